@@ -1,0 +1,149 @@
+/* xtagger_b200: B200-native (sm_100a) EVA02-Large tagger forward behind xTagger's engine C ABI.
+ *
+ * Two layers of entry points, all plain C (pointers and sizes, no torch types):
+ *
+ *  1. The engine (eva_*): a drop-in for the wd engine of HoloArchivists/xTagger, src/engine/eva.h. Same names,
+ *     same argument meaning, same 0 / -1 / NULL error convention with an "eva: ..." line on stderr, same
+ *     ownership rules. xtag.c, the router (procimg.h) and tag stealing (steal.h) call exactly these.
+ *  2. Kernel-level entry points (xtb_*): one per hot-path kernel, device pointers in, enqueued on a caller
+ *     stream, no allocation. The parity tests drive these; they have no counterpart in the reference, which
+ *     launches its kernels only from inside eva.h.
+ *
+ * Input contract per model input (eva.h:15-16): fp16 [1024 patches][592], column c*196 + ky*14 + kx, BGR,
+ * (x/127.5 - 1), columns 588..591 zero.
+ */
+#ifndef XTAGGER_B200_H
+#define XTAGGER_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Constants the callers use (values kept from eva.h:38-69). */
+#ifndef EVA_NB
+#define EVA_NB 8                              /* model inputs per submit (eva.h:38-40) */
+#endif
+#define EVA_NBUF 8                            /* host output slots (eva.h:41) */
+#define EVA_S 448
+#define EVA_D 1024
+#define EVA_T 1025
+#define EVA_NP 1024
+#define EVA_HIDP 2736
+#define EVA_K0P 592
+#define EVA_NL 24
+#define EVA_NH 16
+#define EVA_IN ((size_t)EVA_NP * EVA_K0P)     /* halves per model input (eva.h:57) */
+#define EVA_HB_OFF 0xC1800000u                /* -16.0f: bias of an extra head row nothing has written (eva.h:69) */
+#define EVA_MAXDEV 8
+
+/* Engine handle. Caller-allocated like the reference's `eva` (eva.h:117-151); the fields below are the ones the
+ * reference's callers read (nt: procimg.h:1689, hpn[buf]: procimg.h:1983) plus the batch size. Everything else
+ * lives behind impl. */
+typedef struct eva {
+    uint32_t nt, ntp, nt0;                    /* tags: nt = nt0 of the file + extra rows (tag stealing) */
+    uint32_t nb;                              /* model inputs per submit (EVA_NB, or eva_open_ex's nb) */
+    float *hout[EVA_NBUF];                    /* per slot: scores [nb][nt] fp32, engine-owned */
+    uint16_t *hpn[EVA_NBUF];                  /* per slot, with extra rows: head inputs [nb][1024] fp16 */
+    void *impl;
+} eva;
+
+/* Replaces eva_open (eva.h:573-604). Validates the header of `weights` (eva02.bin v3 per-tensor E4M3, or the
+ * block-scaled v4 this library adds) and returns at once; the CUDA bring-up (weights, buffers, CUDA graph) runs on
+ * its own thread. `pool` (poolb bytes) is the caller's input pool, page-locked in place by the bring-up and still
+ * caller-owned. `extra` head rows past the file's tags (written later with eva_head_put) also enable the per-batch
+ * copy of the head inputs into hpn. 0, or -1 with a stderr line. */
+int eva_open(eva *e, const char *weights, int device, void *pool, size_t poolb, uint32_t extra);
+
+/* Multi-GPU variant (no counterpart in the reference, which drives one GPU): one engine replica per listed
+ * device, each submit's inputs split into contiguous shards, one per device, scores gathered into one hout[buf].
+ * nb = model inputs per submit over all devices (0 = EVA_NB). ndev = -1 with devices NULL: all visible devices. */
+int eva_open_ex(eva *e, const char *weights, const int *devices, int ndev, uint32_t nb, void *pool, size_t poolb,
+                uint32_t extra);
+
+/* Replaces eva_ready (eva.h:607-617): join the bring-up once. 0 or -1. */
+int eva_ready(eva *e);
+/* Replaces eva_poll (eva.h:620-623): 1 once the bring-up has finished. */
+int eva_poll(eva *e);
+/* Replaces eva_submit (eva.h:627-641): n <= nb inputs (pointers, EVA_IN halves each; adjacent ones go in one
+ * copy) into slot buf < EVA_NBUF. Async: H2D, forward graph, D2H into hout[buf] (+ hpn[buf]). Do not resubmit buf
+ * before eva_wait(buf). */
+int eva_submit(eva *e, uint32_t buf, uint16_t *const *in, uint32_t n);
+/* Replaces eva_query (eva.h:662-665): 1 if slot buf is done (or failed). */
+int eva_query(eva *e, uint32_t buf);
+/* Replaces eva_wait (eva.h:667-680): blocking (sleeping) wait; engine-owned [n][nt] scores or NULL on error. */
+const float *eva_wait(eva *e, uint32_t buf);
+/* Replaces eva_head_put (eva.h:645-650): stream-ordered write of head row j (fp16 [1024] + bias); later submits
+ * see it, w may be reused at once. With an FP8 head the row is quantised with its row block's scales. */
+int eva_head_put(eva *e, uint32_t j, const uint16_t *w, float bias);
+/* Replaces eva_head_get (eva.h:653-659): blocking read of the file's nt0 head rows (fp16) and biases. */
+int eva_head_get(eva *e, uint16_t *w, float *bias);
+/* Replaces eva_close (eva.h:704-745): join, sync, unregister the pool, free everything. Safe after a failed open. */
+void eva_close(eva *e);
+
+/* ---- engine extensions (no counterpart in the reference) ---- */
+/* Run the forward graph on inputs already resident on the devices (uploaded by eva_upload), no host copies.
+ * Used to time the device-resident throughput. */
+int eva_forward_resident(eva *e);
+/* Copy n inputs to the devices' input buffers (same sharding as eva_submit), synchronously. */
+int eva_upload(eva *e, uint16_t *const *in, uint32_t n);
+/* Scores of the last resident forward into out [n][nt] (synchronous). */
+int eva_download(eva *e, float *out, uint32_t n);
+/* The CUDA stream (cudaStream_t) the engine uses on its i-th device; NULL if out of range. */
+void *eva_stream(eva *e, int i);
+/* Number of kernel launches in one forward on one device. */
+int eva_launches_per_forward(eva *e);
+/* One direct (non-graph) forward on device 0 with an event after every kernel; per-kernel-kind milliseconds into
+ * ms[kinds] (names from eva_prof_name), returns the number of kinds or -1. Mirrors the reference's EVA_PROF
+ * probe (eva.h:312-339). */
+int eva_profile(eva *e, float *ms, int kinds);
+const char *eva_prof_name(int kind);
+
+/* ---- kernel-level entry points (device pointers, enqueued on `stream`, no allocation) ---- */
+/* D[m][n] fp32 = ascale * sum_kb wscale[n/128][kb] * sum_{k in kb} e4m3(A[m][k]) * e4m3(W[n][k]).
+ * A: E4M3 [m][k], W: E4M3 [n][k], wscale: fp32 [ceil(n/128)][ceil(k/128)], k a multiple of 16. */
+int xtb_gemm_e4m3_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, const float *wscale, float ascale,
+                      float *out, void *stream);
+
+/* LayerNorm over 1024 (eps 1e-6) * g + b, * qs, E4M3: x fp16 [rows][1024] -> y [rows][1024]. Replaces k_ln
+ * (kern_common.cuh:147-186). */
+int xtb_ln_e4m3(const uint16_t *x, const float *g, const float *b, uint8_t *y, int rows, float qs, void *stream);
+/* QKV projection with its attention-layout epilogue; rows = images * 1025. q8 / k8 [img][16][1152][64],
+ * vt8 [img][16][64][1152] (pads must be zero). Replaces k_qkv (eva_kernels.cu:41-114). */
+int xtb_qkv(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *q8, uint8_t *k8,
+            uint8_t *vt8, const float *cs, float cq, float ck, float cv, void *stream);
+/* FP8 attention: out E4M3 [img * 1025][1024] (head h at column 64 h). Replaces k_flash / flash8
+ * (eva_kernels.cu:116-122, kern_common.cuh:403-543). */
+int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, uint8_t *out, float sinv, float vo,
+                  void *stream);
+/* x fp16 [rows][1024] += ascale * a . Wo^T (block-scaled). Replaces k_oproj (eva_kernels.cu:134-162). */
+int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, void *stream);
+/* fc1 + SwiGLU: h8 E4M3 [rows][2736], stat fp32 [43][rows][2] row-statistics partials. Replaces k_fc1
+ * (eva_kernels.cu:211-279). */
+int xtb_fc1(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *h8, float *stat,
+            const float *rs, void *stream);
+/* fc2 with the MLP LayerNorm folded in: x += rstd (acc - mean c) + d. Replaces k_fc2 (eva_kernels.cu:286-334). */
+int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, const float *stat,
+            const float *c, const float *d, void *stream);
+/* Patch embedding (fp16 tcgen05 GEMM) + position rows: in [img][1024][592] fp16 -> x [img][1025][1024] fp16.
+ * Replaces k_pe + k_embed (eva_kernels.cu:21-33, 126-130). */
+int xtb_patch_embed(const uint16_t *in, int nimg, const uint16_t *pe, const float *pos, uint16_t *x, void *stream);
+/* Mean pool over patch tokens + fc_norm -> pn fp16 [img][1024] (pn8 = E4M3(pn * qs) if not NULL). Replaces
+ * k_pool + k_lnh (eva_kernels.cu:404-431, kern_common.cuh:188-192). */
+int xtb_pool_ln(const uint16_t *x, int nimg, const float *g, const float *b, float *pool, uint16_t *pn, uint8_t *pn8,
+                float qs, void *stream);
+/* Tag head + sigmoid: out [img][nt]. fp16 head replaces k_headmv (kern_common.cuh:695-727); the E4M3
+ * block-scaled head (hws [ceil(nt/128)][8]) has no counterpart in the reference. */
+int xtb_head_f16(const uint16_t *hw, int nt, const uint16_t *pn, int nimg, const float *hb, float *out, void *stream);
+int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *pn8, int nimg, float ascale,
+                  const float *hb, float *out, void *stream);
+
+/* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). */
+uint32_t xtb_error_word(int device);
+void xtb_error_clear(int device);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

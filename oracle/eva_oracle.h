@@ -1,0 +1,67 @@
+/* CPU oracle of the EVA02-L tagger forward — TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C (C11 + OpenMP) restatement of the reference's algorithm for the hot path (HoloArchivists/xTagger,
+ * src/engine/eva.h + eva_kernels.cu + kern_common.cuh), used as the checker by tests/, by
+ * __graft_entry__.smoke() and as bench.py's CPU baseline. Nothing in the shipped library links or calls it.
+ * Each function cites the reference lines it restates. Parity pins: see tests/test_oracle_pins.py.
+ */
+#ifndef EVA_ORACLE_H
+#define EVA_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#define OR_D 1024
+#define OR_T 1025
+#define OR_NP 1024
+#define OR_HID 2730
+#define OR_HIDP 2736
+#define OR_K0P 592
+#define OR_NH 16
+#define OR_HD 64
+#define OR_TP 1152
+#define OR_N12 (2 * OR_HIDP)
+
+/* numeric formats */
+uint8_t or_e4m3(float x);                     /* OCP E4M3: round to nearest even, saturate to +-448, NaN -> 0x7F */
+float or_e4m3_dec(uint8_t b);
+void or_e4m3_n(const float *x, uint8_t *y, size_t n);
+void or_e4m3_dec_n(const uint8_t *x, float *y, size_t n);
+uint16_t or_f2h(float x);                     /* IEEE binary16, round to nearest even */
+float or_h2f(uint16_t h);
+void or_f2h_n(const float *x, uint16_t *y, size_t n);
+void or_h2f_n(const uint16_t *x, float *y, size_t n);
+
+/* out[m][n] = ascale * sum_kb ws[n/128][kb] * sum_{k in kb} e4m3(a[m][k]) e4m3(w[n][k]) */
+void or_gemm_e4m3(const uint8_t *a, int m, int k, const uint8_t *w, int n, const float *ws, float ascale, float *out);
+/* out[m][n] = sum_k h(a[m][k]) h(w[n][k]) (fp16 operands, fp32 result) */
+void or_gemm_f16(const uint16_t *a, int m, int k, const uint16_t *w, int n, float *out);
+
+/* forward pieces */
+void or_ln_e4m3(const uint16_t *x, const float *g, const float *b, int rows, float qs, uint8_t *y);
+void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, float ck, float cv, uint8_t *q8,
+                     uint8_t *k8, uint8_t *vt8);
+void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, float sinv, float vo,
+                  int key_tile, uint8_t *out);
+void or_resid_add(uint16_t *x, const float *acc, int rows);
+void or_fc1_epilogue(const float *acc, int rows, const float *rs, uint8_t *h8, double *rowsum, double *rowsq);
+void or_fc2_epilogue(uint16_t *x, const float *acc, int rows, const double *rowsum, const double *rowsq,
+                     const float *c, const float *d);
+void or_patch_embed(const uint16_t *in, int nimg, const uint16_t *pe, const float *pos, uint16_t *x);
+void or_pool_ln(const uint16_t *x, int nimg, const float *g, const float *b, float *pool, uint16_t *pn, uint8_t *pn8,
+                float qs);
+void or_head_f16(const uint16_t *pn, int nimg, const uint16_t *hw, const float *hb, int nt, float *out);
+void or_head_e4m3(const uint8_t *pn8, int nimg, const uint8_t *hw8, const float *hws, float ascale, const float *hb,
+                  int nt, float *out);
+
+/* whole forward from a model file (eva02.bin v3 or the block-scaled v4); in: nimg x [1024][592] fp16.
+ * scores [nimg][nt]; pn (optional) [nimg][1024] fp16. key_tile: 128 (this library's attention tiling) or 64
+ * (the reference's). Returns 0, or -1 with a message on stderr. */
+int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, float *scores, uint16_t *pn);
+/* number of tags of a model file (-1 on error) */
+int or_model_nt(const char *model);
+
+/* 2:4 selection of prune24.py (magnitude or Wanda score): zero the 2 least important of every 4 consecutive k */
+void or_prune24(uint8_t *w, int n, int k, int wanda);
+
+int or_threads(void);
+#endif

@@ -1,0 +1,146 @@
+// Kernel-level C ABI: one entry point per hot-path kernel, device pointers in, stream-ordered, no allocation.
+// These are what the parity tests drive; the engine (engine.cpp) strings the same launchers into a CUDA graph.
+#include "../../include/xtagger_b200.h"
+#include "host.h"
+#include "ops.h"
+
+using namespace xtb;
+
+static cudaStream_t S(void *s)
+{
+    prepare_kernels();  // once per device; cheap afterwards
+    return (cudaStream_t)s;
+}
+
+extern "C" {
+
+int xtb_gemm_e4m3_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, const float *wscale, float ascale,
+                      float *out, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (m <= 0 || n <= 0 || k <= 0 || (k & 15)) {
+        fprintf(stderr, "eva: xtb_gemm_e4m3_f32: bad shape m %d n %d k %d (k must be a multiple of 16)\n", m, n, k);
+        return -1;
+    }
+    if (make_operand(&A, a, m, k, 128) || make_operand(&W.op, w, n, k, 256)) return -1;
+    W.ws = wscale;
+    W.n = n;
+    W.k = k;
+    return launch_gemm_f32(A, W, ascale, out, n, S(stream));
+}
+
+static int rows_ok(int rows, const char *what)
+{
+    if (rows <= 0) {
+        fprintf(stderr, "eva: %s: bad row count %d\n", what, rows);
+        return 0;
+    }
+    return 1;
+}
+
+static int weight(Weight8 *w, const uint8_t *p, int n, int k, const float *ws)
+{
+    w->ws = ws;
+    w->n = n;
+    w->k = k;
+    return make_operand(&w->op, p, n, k, 256);
+}
+
+int xtb_ln_e4m3(const uint16_t *x, const float *g, const float *b, uint8_t *y, int rows, float qs, void *stream)
+{
+    if (!rows_ok(rows, "xtb_ln_e4m3")) return -1;
+    return launch_ln_e4m3((const __half *)x, g, b, y, rows, qs, S(stream));
+}
+
+int xtb_qkv(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *q8, uint8_t *k8,
+            uint8_t *vt8, const float *cs, float cq, float ck, float cv, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (!rows_ok(rows, "xtb_qkv") || make_operand(&A, h, rows, D, 128) || weight(&W, w, 3 * D, D, ws)) return -1;
+    return launch_qkv(A, W, ascale, rows, q8, k8, vt8, cs, cq, ck, cv, S(stream));
+}
+
+int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, uint8_t *out, float sinv, float vo,
+                  void *stream)
+{
+    Attn a;
+    if (nimg <= 0 || make_attn(&a, q8, k8, vt8, nimg)) return -1;
+    return launch_attention(a, nimg, out, sinv, vo, S(stream));
+}
+
+int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (!rows_ok(rows, "xtb_oproj") || make_operand(&A, a, rows, D, 128) || weight(&W, w, D, D, ws)) return -1;
+    return launch_oproj(A, W, ascale, rows, (__half *)x, S(stream));
+}
+
+int xtb_fc1(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *h8, float *stat,
+            const float *rs, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (!rows_ok(rows, "xtb_fc1") || make_operand(&A, h, rows, D, 128) || weight(&W, w, N12, D, ws)) return -1;
+    return launch_fc1(A, W, ascale, rows, h8, (float2 *)stat, rs, S(stream));
+}
+
+int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, const float *stat,
+            const float *c, const float *d, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (!rows_ok(rows, "xtb_fc2") || make_operand(&A, h8, rows, HIDP, 128) || weight(&W, w, D, HIDP, ws)) return -1;
+    return launch_fc2(A, W, ascale, rows, (__half *)x, (const float2 *)stat, c, d, S(stream));
+}
+
+int xtb_patch_embed(const uint16_t *in, int nimg, const uint16_t *pe, const float *pos, uint16_t *x, void *stream)
+{
+    Operand A, B;
+    if (nimg <= 0 || make_operand(&A, in, nimg * NP, K0P * 2, 128) || make_operand(&B, pe, D, K0P * 2, 256)) return -1;
+    return launch_patch_embed(A, B, nimg, pos, (__half *)x, S(stream));
+}
+
+int xtb_pool_ln(const uint16_t *x, int nimg, const float *g, const float *b, float *pool, uint16_t *pn, uint8_t *pn8,
+                float qs, void *stream)
+{
+    if (nimg <= 0) return -1;
+    return launch_pool_ln((const __half *)x, nimg, g, b, pool, (__half *)pn, pn8, qs, S(stream));
+}
+
+int xtb_head_f16(const uint16_t *hw, int nt, const uint16_t *pn, int nimg, const float *hb, float *out, void *stream)
+{
+    Operand A, B;
+    if (nt <= 0 || nimg <= 0 || make_operand(&A, hw, nt, D * 2, 128) || make_operand(&B, pn, nimg, D * 2, 64)) return -1;
+    return launch_head_f16(A, B, nimg, nt, hb, out, S(stream));
+}
+
+int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *pn8, int nimg, float ascale,
+                  const float *hb, float *out, void *stream)
+{
+    Weight8 W;
+    Operand B;
+    if (nt <= 0 || nimg <= 0) return -1;
+    W.ws = hws;
+    W.n = nt;
+    W.k = D;
+    if (make_operand(&W.op, hw8, nt, D, 128) || make_operand(&B, pn8, nimg, D, 64)) return -1;
+    return launch_head_e4m3(W, B, ascale, nimg, nt, hb, out, S(stream));
+}
+
+uint32_t xtb_error_word(int device)
+{
+    uint32_t *p = error_word(device), v = 0;
+    if (p && cudaMemcpy(&v, p, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return 0xFFFFFFFFu;
+    return v;
+}
+
+void xtb_error_clear(int device)
+{
+    uint32_t *p = error_word(device);
+    if (p) cudaMemset(p, 0, 4);
+}
+
+}  // extern "C"

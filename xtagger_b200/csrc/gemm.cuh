@@ -1,0 +1,257 @@
+// Block-scaled FP8 (and fp16) GEMM on tcgen05 for sm_100a:  D[M][N] = epilogue( sum_k A[m][k] * B[n][k] ).
+//
+// One persistent CTA per SM walks output tiles of 128 x BN. Warp roles (320 threads):
+//   warp 0      TMA producer: 128-byte-wide K slices of A (128 rows) and B (BN rows), 128B-swizzled, into a
+//               STAGES-deep shared-memory ring guarded by full/empty mbarriers.
+//   warp 1      allocates TMEM (512 columns) and one elected lane issues tcgen05.mma (M = 128, N = BN, K = 32 bytes
+//               per instruction, 4 instructions per 128-byte slice).
+//   warps 2..9  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..; two warps per lane
+//               quadrant split the BN columns), apply the fused epilogue, store through a per-warp 4 KB staging
+//               buffer so that global stores are whole 128-byte rows (or 32-byte sectors) per warp instruction.
+//
+// PROMOTE (FP8 weights with one fp32 scale per 128 x 128 block): every 128-element K block is accumulated into its
+// own TMEM buffer (two buffers of BN columns, ping-pong), and the epilogue warps fold it into fp32 registers with
+// acc += (a_scale * w_scale[block]) * partial (packed fma.rn.f32x2). This keeps the dequantize-then-matmul
+// semantics exactly (scales are arbitrary fp32, not powers of two) while the tensor core runs the next K block into
+// the other buffer. Without PROMOTE the whole K range accumulates in one TMEM buffer; the buffers ping-pong across
+// tiles so that the epilogue of one tile overlaps the main loop of the next.
+#pragma once
+#include "ptx.cuh"
+
+namespace xtb {
+
+struct GemmArgs {
+    int M, N;            // output rows / columns (rows of A / rows of B)
+    int kiters;          // 128-byte K slices (ceil(K bytes / 128))
+    int m_tiles, n_tiles;
+    const float *ws;     // PROMOTE: block scales [ws_rows][ws_ld]; row = N block (or M block when WS_ON_M)
+    int ws_ld, ws_rows;
+    float ascale;        // activation dequant scale, folded into every block scale (PROMOTE only)
+    uint32_t *err;       // library error word
+};
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int COLS = BN / 2;  // accumulator columns per epilogue thread
+    static constexpr int STAGING = 8 * 4096;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + STAGING + 256;
+    static constexpr int THREADS = 320;
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+// Epilogue context of one thread: output row row0 + lane, columns col0 .. col0 + COLS - 1.
+struct EpiCtx {
+    int row0;        // first row of this warp's 32 rows
+    int col0;
+    int lane;
+    uint8_t *stage;  // this warp's 4 KB staging buffer: 32 rows x 128 bytes, 16-byte chunks XOR-swizzled by row
+};
+
+// Staging helpers. Row r's 16-byte chunk c sits at r * 128 + ((c ^ (r & 7)) * 16): a warp writing one row per lane
+// and a warp reading one row across lanes are both free of bank conflicts.
+__device__ __forceinline__ uint8_t *stage_chunk(uint8_t *st, int r, int c) { return st + r * 128 + (((c ^ (r & 7)) & 7) << 4); }
+__device__ __forceinline__ void stage_row_f32(uint8_t *st, int lane, const float *v)
+{
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+        *(float4 *)stage_chunk(st, lane, c) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+__device__ __forceinline__ float stage_f32(uint8_t *st, int r, int w) { return *(const float *)(stage_chunk(st, r, w >> 2) + ((w & 3) << 2)); }
+__device__ __forceinline__ float2 stage_f32x2(uint8_t *st, int r, int w) { return *(const float2 *)(stage_chunk(st, r, w >> 2) + ((w & 3) << 2)); }
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    uint64_t d = *reinterpret_cast<uint64_t *>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+
+template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
+__global__ void __launch_bounds__(320, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g,
+           const typename Epi::Params ep)
+{
+    using C = GemmCfg<BN>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int COLS = C::COLS;
+    constexpr uint32_t IDESC = idesc_m128(BN);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * C::A_BYTES;
+    uint8_t *sStage = smem + STAGES * C::STAGE_BYTES;
+    uint64_t *full = (uint64_t *)(sStage + C::STAGING);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tslot = (uint32_t *)(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);
+        }
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tslot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    const int total = g.m_tiles * g.n_tiles;
+    const int KI = g.kiters;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                const int mb = t % g.m_tiles, nb = t / g.m_tiles;
+                for (int k = 0; k < KI; k++) {
+                    if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], k * 128, mb * 128);
+                    tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], k * 128, nb * BN);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t ph = 0, tb = 0, tph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int k = 0; k < KI; k++) {
+                    if (PROMOTE || k == 0) {
+                        if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
+                        tc_fence_after();
+                    }
+                    if (!(ok = mbar_wait(&full[stage], ph, g.err, XTB_ERR_WAIT_TMA))) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+                    const uint32_t d = tbase + tb * BN;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        umma<F16>(d, sdesc(a0 + kk * 32, 1024, SWZ_128B), sdesc(b0 + kk * 32, 1024, SWZ_128B), IDESC,
+                                  PROMOTE ? (kk > 0) : (k > 0 || kk > 0));
+                    umma_commit(&empty[stage]);
+                    if (PROMOTE || k == KI - 1) {
+                        umma_commit(&tfull[tb]);
+                        tb ^= 1;
+                        if (!tb) tph ^= 1;
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+        }
+    } else {
+        const int ew = warp - 2;
+        const int quad = warp & 3;
+        const int half = ew >> 2;
+        EpiCtx cx;
+        cx.lane = lane;
+        cx.stage = sStage + ew * 4096;
+        uint32_t tb = 0, tph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            const int mb = t % g.m_tiles, nb = t / g.m_tiles;
+            cx.row0 = mb * 128 + quad * 32;
+            cx.col0 = nb * BN + half * COLS;
+            float2 acc[COLS / 2];
+#pragma unroll
+            for (int j = 0; j < COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);
+            const int units = PROMOTE ? KI : 1;
+            const float *wsr = nullptr;
+            if (PROMOTE) wsr = g.ws + (size_t)min(WS_ON_M ? mb : (cx.col0 >> 7), g.ws_rows - 1) * g.ws_ld;
+            for (int u = 0; u < units; u++) {
+                // warp-uniform outcome: the tcgen05.ld below is a .sync.aligned warp instruction
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
+                tc_fence_after();
+                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * BN + half * COLS;
+                const float s = PROMOTE ? g.ascale * __ldg(wsr + u) : 1.0f;
+                const float2 s2 = make_float2(s, s);
+#pragma unroll
+                for (int c = 0; c < COLS / 32; c++) {
+                    float v[32];
+                    tmem_ld32(taddr + c * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (PROMOTE) acc[c * 16 + j] = ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[c * 16 + j]);
+                        else acc[c * 16 + j] = make_float2(v[2 * j], v[2 * j + 1]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[tb]);
+                tb ^= 1;
+                if (!tb) tph ^= 1;
+            }
+            if (!ok) break;
+            Epi::apply(ep, (float *)acc, cx);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Epilogues: apply(params, acc[COLS], ctx). acc holds output row ctx.row0 + lane, columns ctx.col0 .. + COLS - 1
+// (already dequantised when the GEMM promotes block scales). Rows / columns past the problem are skipped.
+// ---------------------------------------------------------------------------------------------------------------
+
+// Plain fp32 store: out[row][col] (row stride ld floats). Used for the stand-alone block-scaled GEMM.
+template <int COLS>
+struct EpiF32 {
+    struct Params {
+        float *out;
+        int ld, M, N;
+    };
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    {
+#pragma unroll
+        for (int c = 0; c < COLS / 32; c++) {
+            __syncwarp();
+            stage_row_f32(cx.stage, cx.lane, acc + 32 * c);
+            __syncwarp();
+            const int col = cx.col0 + 32 * c + cx.lane;
+            if (col < p.N) {
+#pragma unroll 4
+                for (int i = 0; i < 32; i++) {
+                    const int row = cx.row0 + i;
+                    if (row < p.M) p.out[(size_t)row * p.ld + col] = stage_f32(cx.stage, i, cx.lane);
+                }
+            }
+        }
+        __syncwarp();
+    }
+};
+
+}  // namespace xtb

@@ -1,0 +1,30 @@
+// Host-side helpers shared by the launchers and the engine: error reporting in the engine's "eva: ..." style,
+// TMA tensor-map encoding (through the driver entry point, so the library needs no -lcuda), SM count cache.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+namespace xtb {
+
+#define XTB_CK(call)                                                                             \
+    do {                                                                                         \
+        cudaError_t e_ = (call);                                                                 \
+        if (e_ != cudaSuccess) {                                                                 \
+            fprintf(stderr, "eva: %s: %s (%s:%d)\n", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return -1;                                                                           \
+        }                                                                                        \
+    } while (0)
+
+// 2D byte matrix [rows][cols bytes] (row pitch `pitch` bytes, a multiple of 16) read in boxes of
+// box_cols bytes x box_rows rows with the given swizzle. Out-of-range boxes read as zero.
+int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t box_cols,
+                 uint32_t box_rows, CUtensorMapSwizzle swz);
+
+int num_sms(int device);
+
+// Library error word on the given device (set by kernels whose bounded waits ran out).
+uint32_t *error_word(int device);
+
+}  // namespace xtb

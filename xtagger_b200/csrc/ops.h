@@ -1,0 +1,61 @@
+// Internal C++ interface between the engine and the kernel launchers (ops.cu). Every launcher returns 0 or -1
+// (with an "eva: ..." line on stderr) and only enqueues work on the given stream: no allocation, no sync.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xtb {
+
+// Model shapes (EVA02-Large tagger, 448^2 input, patch 14).
+constexpr int D = 1024, T = 1025, NP = 1024, HID = 2730, HIDP = 2736, K0P = 592, NH = 16, HD = 64;
+constexpr int N12 = 2 * HIDP;                     // fc1 output rows (g / x interleaved in 16-unit chunks)
+constexpr int NSTAT = (N12 + 127) / 128;          // fc1 row-statistics partials per row (one per 128 fc1 columns)
+constexpr int TP = 1152;                          // attention keys per (image, head), padded to 9 x 128
+constexpr int QT = (T + 127) / 128;               // 128-query tiles per (image, head)
+
+// Prepared operand: a row-major byte matrix plus its TMA descriptor (box = 128 bytes x box_rows, 128B swizzle).
+struct Operand {
+    CUtensorMap map;
+    const void *ptr;
+    int rows, row_bytes;
+};
+int make_operand(Operand *op, const void *ptr, int rows, int row_bytes, int box_rows);
+
+// Block-scaled weight: E4M3 [n][k] plus fp32 scales [ceil(n / 128)][ceil(k / 128)].
+struct Weight8 {
+    Operand op;
+    const float *ws;
+    int n, k;
+};
+
+struct Attn {
+    CUtensorMap tq, tk, tv;
+};
+
+// ---- launchers (device pointers; stream-ordered) ----
+int launch_gemm_f32(const Operand &a, const Weight8 &w, float ascale, float *out, int ldo, cudaStream_t st);
+int launch_patch_embed(const Operand &in, const Operand &pe, int nimg, const float *pos, __half *x, cudaStream_t st);
+int launch_ln_e4m3(const __half *x, const float *g, const float *b, uint8_t *y, int rows, float qs, cudaStream_t st);
+int launch_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *q8, uint8_t *k8, uint8_t *vt8,
+               const float *cs, float cq, float ck, float cv, cudaStream_t st);
+int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg);
+int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st);
+int launch_oproj(const Operand &a, const Weight8 &w, float ascale, int rows, __half *x, cudaStream_t st);
+int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
+               cudaStream_t st);
+int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, const float2 *stat,
+               const float *c, const float *d, cudaStream_t st);
+int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
+                   float qs_head, cudaStream_t st);
+int launch_head_f16(const Operand &hw, const Operand &pn, int nimg, int nt, const float *hb, float *out,
+                    cudaStream_t st);
+int launch_head_e4m3(const Weight8 &hw, const Operand &pn8, float ascale, int nimg, int nt, const float *hb, float *out,
+                     cudaStream_t st);
+
+int current_device();
+// Shared-memory opt-in of every kernel on the current device (call before any stream capture).
+int prepare_kernels();
+
+}  // namespace xtb

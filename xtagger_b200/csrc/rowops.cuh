@@ -1,0 +1,136 @@
+// Memory-bound row kernels of the forward: LayerNorm + E4M3 quantisation of the GEMM inputs, mean pooling over
+// patch tokens, and the fc_norm LayerNorm that produces the head input.
+#pragma once
+#include "ops.h"
+#include "ptx.cuh"
+
+namespace xtb {
+
+// LayerNorm over 1024 fp16 values (eps 1e-6, two-pass mean / variance from registers), * gamma + beta, * qs,
+// E4M3 with saturation. One warp per row, 8 rows per 256-thread block; 16-byte loads, 8-byte stores.
+// Replaces k_ln / ln_row<1> (kern_common.cuh:147-186).
+__global__ void __launch_bounds__(256) k_ln_e4m3(const __half *__restrict__ x, const float *__restrict__ g,
+                                                 const float *__restrict__ bta, uint8_t *__restrict__ y, int rows,
+                                                 float qs)
+{
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const uint4 *xr = (const uint4 *)(x + (size_t)row * D);
+    float v[32];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint4 u = xr[lane + 32 * i];
+        const __half2 *hp = (const __half2 *)&u;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(hp[e]);
+            v[8 * i + 2 * e] = f.x;
+            v[8 * i + 2 * e + 1] = f.y;
+            s += f.x + f.y;
+        }
+    }
+    const float mean = warp_sum(s) * (1.0f / D);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const float dx = v[i] - mean;
+        q += dx * dx;
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
+    uint2 *yr = (uint2 *)(y + (size_t)row * D);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int c = 8 * (lane + 32 * i);
+        const float4 g0 = *(const float4 *)(g + c), g1 = *(const float4 *)(g + c + 4);
+        const float4 b0 = *(const float4 *)(bta + c), b1 = *(const float4 *)(bta + c + 4);
+        const float *w = v + 8 * i;
+        float o[8];
+        o[0] = (w[0] - mean) * rstd * g0.x + b0.x;
+        o[1] = (w[1] - mean) * rstd * g0.y + b0.y;
+        o[2] = (w[2] - mean) * rstd * g0.z + b0.z;
+        o[3] = (w[3] - mean) * rstd * g0.w + b0.w;
+        o[4] = (w[4] - mean) * rstd * g1.x + b1.x;
+        o[5] = (w[5] - mean) * rstd * g1.y + b1.y;
+        o[6] = (w[6] - mean) * rstd * g1.z + b1.z;
+        o[7] = (w[7] - mean) * rstd * g1.w + b1.w;
+        yr[lane + 32 * i] = make_uint2(e4m3x2(o[0] * qs, o[1] * qs) | (e4m3x2(o[2] * qs, o[3] * qs) << 16),
+                                       e4m3x2(o[4] * qs, o[5] * qs) | (e4m3x2(o[6] * qs, o[7] * qs) << 16));
+    }
+}
+
+// Mean over patch tokens 1..1024 of each image: x [img][1025][1024] fp16 -> pool [img][1024] fp32.
+// Grid (img, 16): 64 columns per block; thread (c, grp) sums 4 columns over a 64-token group; the 16 group
+// partials are added in a fixed order. Replaces k_pool (eva_kernels.cu:404-431).
+__global__ void __launch_bounds__(256) k_pool(const __half *__restrict__ x, float *__restrict__ pool)
+{
+    __shared__ float4 red[16][16];
+    const int c = threadIdx.x & 15, grp = threadIdx.x >> 4;
+    const __half *xr = x + ((size_t)blockIdx.x * T + 1 + grp * 64) * D + blockIdx.y * 64 + 4 * c;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int t = 0; t < 64; t++) {
+        const uint2 u = *(const uint2 *)(xr + (size_t)t * D);
+        const float2 p = __half22float2(*(const __half2 *)&u.x), q = __half22float2(*(const __half2 *)&u.y);
+        a.x += p.x;
+        a.y += p.y;
+        a.z += q.x;
+        a.w += q.y;
+    }
+    red[grp][c] = a;
+    __syncthreads();
+    if (grp) return;
+    float4 v = red[0][c];
+    for (int i = 1; i < 16; i++) {
+        const float4 w = red[i][c];
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+    }
+    const float k = 1.0f / (T - 1);
+    *(float4 *)(pool + (size_t)blockIdx.x * D + blockIdx.y * 64 + 4 * c) = make_float4(v.x * k, v.y * k, v.z * k, v.w * k);
+}
+
+// fc_norm LayerNorm of the pooled features -> fp16 head input pn (and, for an FP8 head, E4M3(pn * qs)).
+// One warp per image. Replaces k_lnh (kern_common.cuh:188-192).
+__global__ void __launch_bounds__(256) k_ln_head(const float *__restrict__ pool, const float *__restrict__ g,
+                                                 const float *__restrict__ bta, __half *__restrict__ pn,
+                                                 uint8_t *__restrict__ pn8, int nimg, float qs)
+{
+    const int img = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (img >= nimg) return;
+    const float4 *xr = (const float4 *)(pool + (size_t)img * D);
+    float4 v[8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        v[i] = xr[lane + 32 * i];
+        s += v[i].x + v[i].y + v[i].z + v[i].w;
+    }
+    const float mean = warp_sum(s) * (1.0f / D);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float dx;
+        dx = v[i].x - mean; q += dx * dx;
+        dx = v[i].y - mean; q += dx * dx;
+        dx = v[i].z - mean; q += dx * dx;
+        dx = v[i].w - mean; q += dx * dx;
+    }
+    const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int c = 4 * (lane + 32 * i);
+        const float4 gg = *(const float4 *)(g + c), bb = *(const float4 *)(bta + c);
+        const __half2 h0 = __floats2half2_rn((v[i].x - mean) * rstd * gg.x + bb.x, (v[i].y - mean) * rstd * gg.y + bb.y);
+        const __half2 h1 = __floats2half2_rn((v[i].z - mean) * rstd * gg.z + bb.z, (v[i].w - mean) * rstd * gg.w + bb.w);
+        *(uint2 *)(pn + (size_t)img * D + c) = make_uint2(*(const uint32_t *)&h0, *(const uint32_t *)&h1);
+        if (pn8) {
+            const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+            *(uint32_t *)(pn8 + (size_t)img * D + c) = e4m3x2(f0.x * qs, f0.y * qs) | (e4m3x2(f1.x * qs, f1.y * qs) << 16);
+        }
+    }
+}
+
+}  // namespace xtb
