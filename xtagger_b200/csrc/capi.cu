@@ -87,13 +87,13 @@ int xtb_fc1(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float
     return launch_fc1(A, W, ascale, rows, h8, (float2 *)stat, rs, S(stream));
 }
 
-int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, const float *stat,
+int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, float *stat,
             const float *c, const float *d, void *stream)
 {
     Operand A;
     Weight8 W;
     if (!rows_ok(rows, "xtb_fc2") || make_operand(&A, h8, rows, HIDP, 128) || weight(&W, w, D, HIDP, ws)) return -1;
-    return launch_fc2(A, W, ascale, rows, (__half *)x, (const float2 *)stat, c, d, S(stream));
+    return launch_fc2(A, W, ascale, rows, (__half *)x, (float2 *)stat, c, d, S(stream));
 }
 
 int xtb_patch_embed(const uint16_t *in, int nimg, const uint16_t *pe, const float *pos, uint16_t *x, void *stream)

@@ -1,11 +1,15 @@
 // Fused GEMM epilogues of the EVA02-L forward (calling convention in gemm.cuh). Each one replaces a reference
 // kernel's epilogue, written for the tcgen05 GEMM's one-row-per-thread accumulator layout:
 //   EpiQKV    <- k_qkv   (eva_kernels.cu:41-114):  RoPE on q / k of patch tokens, E4M3, attention layouts
-//   EpiResid  <- k_oproj (eva_kernels.cu:134-162): fp16 residual += acc
-//   EpiFC1    <- k_fc1   (eva_kernels.cu:211-279): SwiGLU, per-row LN statistics partials, E4M3 h
-//   EpiFC2    <- k_fc2   (eva_kernels.cu:286-334): inner MLP LayerNorm folded in, fp16 residual += ...
+//   EpiResid  <- k_oproj (eva_kernels.cu:134-162): fp16 residual += acc, as a TMA reduce-add into x
+//   EpiFC1    <- k_fc1   (eva_kernels.cu:211-279): SwiGLU, per-row LN statistics partials, E4M3 h (TMA store)
+//   EpiFC2    <- k_fc2   (eva_kernels.cu:286-334): inner MLP LayerNorm folded in, TMA reduce-add into x
 //   EpiPatch  <- k_pe + k_embed (eva_kernels.cu:21-33, 126-130): patch embedding + position / cls rows
 //   EpiHead   <- k_headmv (kern_common.cuh:695-727): logits + bias -> sigmoid, weights as the M operand
+// The residual updates are asynchronous bulk reductions (cp.reduce.async.bulk.tensor .add on the fp16 residual):
+// the epilogue writes fp16(delta) to shared memory and the TMA unit performs x = fp16(x + fp16(delta)) in L2, so
+// no epilogue thread waits on a load of x. Against the reference's x = fp16(x + delta) this rounds delta to fp16
+// first: at most half an fp16 ulp of delta, far below an ulp of x.
 #pragma once
 #include "gemm.cuh"
 #include "ops.h"
@@ -24,7 +28,9 @@ struct EpiQKV {
         float cq, ck, cv;
         int M;
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    using State = NoState;
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
         const int which = cx.col0 >> 10;           // 0 q, 1 k, 2 v (a thread's 128 columns never straddle)
         const int head0 = (cx.col0 & 1023) >> 6;   // two heads per thread
@@ -86,59 +92,72 @@ struct EpiQKV {
     }
 };
 
-// ---- fp16 residual update: x[row][col] = fp16(x + acc) (attention out-projection) ----
+// ---- fp16 residual update (attention out-projection): x[row][col] += acc, by TMA reduce-add ----
+// 64-column rounds: the warp's 32 rows x 64 fp16 deltas (4 KB, 128B-swizzled like the x tensor map's box) go out
+// as one cp.reduce.async.bulk.tensor.
+template <class F>
+__device__ __forceinline__ void reduce_add_rows(const EpiCtx &cx, int M, int col, F delta)
+{
+    if (cx.lane == 0) bulk_wait_read0();  // the previous round's source has been read
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        __half2 h[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) h[e] = __floats2half2_rn(delta(8 * c + 2 * e), delta(8 * c + 2 * e + 1));
+        *(uint4 *)stage_chunk(cx.stage, cx.lane, c) = *(const uint4 *)h;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (cx.lane == 0 && cx.row0 < M) {
+        tma_reduce_add_2d(cx.tmC, cx.stage, col, cx.row0);
+        bulk_commit();
+    }
+}
+
 struct EpiResid {
     struct Params {
-        __half *x;
         int M;
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    using State = NoState;
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            __syncwarp();
-            stage_row_f32(cx.stage, cx.lane, acc + 32 * c);
-            __syncwarp();
-            const int w = (cx.lane & 15) * 2;
-#pragma unroll 4
-            for (int i = 0; i < 16; i++) {
-                const int r = 2 * i + (cx.lane >> 4), row = cx.row0 + r;
-                if (row < p.M) {
-                    __half2 *xp = (__half2 *)(p.x + (size_t)row * D + cx.col0 + 32 * c + w);
-                    const float2 a = stage_f32x2(cx.stage, r, w);
-                    const float2 xf = __half22float2(*xp);
-                    *xp = __floats2half2_rn(xf.x + a.x, xf.y + a.y);
-                }
-            }
-        }
-        __syncwarp();
+        for (int rd = 0; rd < 2; rd++) reduce_add_rows(cx, p.M, cx.col0 + 64 * rd, [&](int j) { return acc[64 * rd + j]; });
     }
 };
 
 // ---- fc1 + SwiGLU: W12 rows interleave g / x in 16-unit chunks (32 columns = units 16c .. 16c + 15) ----
 // u = x * g * sigmoid(g) (sigmoid(g) = 0.5 (1 + tanh(g / 2)), as the reference), h8 = E4M3(u * rs[unit]),
 // stat[col0 / 128][row] = (sum u, sum u^2) over this thread's 64 units (each partial has exactly one writer).
+// h8 leaves through a TMA store of the warp's 32 rows x 64 units (64-byte rows, 64B swizzle).
 struct EpiFC1 {
     struct Params {
-        uint8_t *h8;
         float2 *stat;
         const float *rs;
         int M;
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    using State = NoState;
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
         const int row = cx.row0 + cx.lane;
+        if (cx.col0 >= N12) return;  // warp-uniform: this half of the last tile is past the units
         float s = 0.f, q = 0.f;
-        int nch = 0;
+        if (cx.lane == 0) bulk_wait_read0();
+        __syncwarp();
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             const int n = cx.col0 + 32 * c;
             if (n >= N12) break;
-            nch = c + 1;
             const int ub = n >> 1;
+            const float4 *rs4 = (const float4 *)(p.rs + ub);
             uint32_t w[4];
 #pragma unroll
             for (int i = 0; i < 16; i += 4) {
+                const float4 r4 = __ldg(rs4 + (i >> 2));
+                const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
                 float hq[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
@@ -146,72 +165,49 @@ struct EpiFC1 {
                     const float u = xx * (0.5f * gg * (1.0f + tanh_fast(0.5f * gg)));
                     s += u;
                     q += u * u;
-                    hq[e] = u * __ldg(p.rs + ub + i + e);
+                    hq[e] = u * rr[e];
                 }
                 w[i >> 2] = e4m3x2(hq[0], hq[1]) | (e4m3x2(hq[2], hq[3]) << 16);
             }
-            *(uint4 *)stage_chunk(cx.stage, cx.lane, c) = make_uint4(w[0], w[1], w[2], w[3]);
+            *(uint4 *)(cx.stage + cx.lane * 64 + ((c ^ ((cx.lane >> 1) & 3)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        if (nch && row < p.M) p.stat[(size_t)(cx.col0 >> 7) * p.M + row] = make_float2(s, q);
+        if (row < p.M) p.stat[(size_t)(cx.col0 >> 7) * p.M + row] = make_float2(s, q);
+        fence_proxy_async_smem();
         __syncwarp();
-        // 32 rows x nch 16-byte chunks; h8 is read once by fc2, so it leaves with an evict-first hint
-        const int ub0 = cx.col0 >> 1;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int pc = i * 32 + cx.lane, r = pc >> 2, ch = pc & 3;
-            const int rw = cx.row0 + r;
-            if (ch < nch && rw < p.M)
-                __stcs((uint4 *)(p.h8 + (size_t)rw * HIDP + ub0 + 16 * ch), *(const uint4 *)stage_chunk(cx.stage, r, ch));
+        if (cx.lane == 0 && cx.row0 < p.M) {
+            tma_store_2d(cx.tmC, cx.stage, cx.col0 >> 1, cx.row0);
+            bulk_commit();
         }
-        __syncwarp();
     }
 };
 
-// ---- fc2 with the MLP LayerNorm folded in: x += rstd * (acc - mean * c) + d ----
-// mean / rstd over the 2730 SwiGLU units from fc1's NSTAT partials of the row, summed in a fixed order.
+// ---- fc2 with the MLP LayerNorm folded in: x += rstd * (acc - mean * c) + d, by TMA reduce-add ----
+// (mean, rstd) of the row over the 2730 SwiGLU units come from k_rowstat, which folds fc1's partials in a fixed
+// order into stat[0][row]; the load is issued when the tile starts.
 struct EpiFC2 {
     struct Params {
-        __half *x;
-        const float2 *stat;
+        const float2 *ms;
         const float *c, *d;
         int M;
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    struct State {
+        float2 ms;
+    };
+    __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &st)
     {
         const int row = cx.row0 + cx.lane;
-        float s = 0.f, q = 0.f;
-        if (row < p.M) {
-#pragma unroll 4
-            for (int g = 0; g < NSTAT; g++) {
-                const float2 v = p.stat[(size_t)g * p.M + row];
-                s += v.x;
-                q += v.y;
-            }
-        }
-        const float mean = s * (1.0f / HID);
-        const float rstd = rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f);
-        const float nb = -mean * rstd;
+        st.ms = row < p.M ? p.ms[row] : make_float2(0.f, 1.f);
+    }
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &st)
+    {
+        const float rstd = st.ms.y, nb = -st.ms.x * st.ms.y;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            __syncwarp();
-            stage_row_f32(cx.stage, cx.lane, acc + 32 * c);
-            __syncwarp();
-            const int w = (cx.lane & 15) * 2;
-            const int col = cx.col0 + 32 * c + w;
-            const float2 c2 = *(const float2 *)(p.c + col), d2 = *(const float2 *)(p.d + col);
-#pragma unroll 4
-            for (int i = 0; i < 16; i++) {
-                const int r = 2 * i + (cx.lane >> 4), rw = cx.row0 + r;
-                const float rs = __shfl_sync(0xffffffffu, rstd, r), bb = __shfl_sync(0xffffffffu, nb, r);
-                if (rw < p.M) {
-                    __half2 *xp = (__half2 *)(p.x + (size_t)rw * D + col);
-                    const float2 a = stage_f32x2(cx.stage, r, w);
-                    const float2 xf = __half22float2(*xp);
-                    *xp = __floats2half2_rn(xf.x + rs * a.x + bb * c2.x + d2.x, xf.y + rs * a.y + bb * c2.y + d2.y);
-                }
-            }
+        for (int rd = 0; rd < 2; rd++) {
+            const int col = cx.col0 + 64 * rd;
+            reduce_add_rows(cx, p.M, col, [&](int j) {
+                return fmaf(rstd, acc[64 * rd + j], fmaf(nb, __ldg(p.c + col + j), __ldg(p.d + col + j)));
+            });
         }
-        __syncwarp();
     }
 };
 
@@ -223,7 +219,9 @@ struct EpiPatch {
         const float *pos;
         int M;  // patch rows = images * 1024
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    using State = NoState;
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
 #pragma unroll
         for (int c = 0; c < 4; c++) {
@@ -261,7 +259,9 @@ struct EpiHead {
         const float *hb;
         int nt, nimg;
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    using State = NoState;
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
         const int tag = cx.row0 + cx.lane;
         if (tag >= p.nt) return;

@@ -37,8 +37,9 @@ struct GemmCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
     static constexpr int COLS = BN / 2;  // accumulator columns per epilogue thread
+    static constexpr int TBUF = 512 / BN;  // TMEM accumulator buffers (512 columns in all)
     static constexpr int STAGING = 8 * 4096;
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + STAGING + 256;
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + STAGING + 512;  // + barriers
     static constexpr int THREADS = 320;
     static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -49,7 +50,11 @@ struct EpiCtx {
     int col0;
     int lane;
     uint8_t *stage;  // this warp's 4 KB staging buffer: 32 rows x 128 bytes, 16-byte chunks XOR-swizzled by row
+    const CUtensorMap *tmC;  // the epilogue's output tensor map (TMA stores / reductions), when it has one
 };
+
+// Epilogues without per-tile state use this.
+struct NoState {};
 
 // Staging helpers. Row r's 16-byte chunk c sits at r * 128 + ((c ^ (r & 7)) * 16): a warp writing one row per lane
 // and a warp reading one row across lanes are both free of bank conflicts.
@@ -71,9 +76,11 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
 }
 
 template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
+// 320 threads put three warps on two of the SM's four sub-partitions (16K registers each): at most 168
+// registers per thread.
 __global__ void __launch_bounds__(320, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs g,
-           const typename Epi::Params ep)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+           const __grid_constant__ CUtensorMap tmC, const GemmArgs g, const typename Epi::Params ep)
 {
     using C = GemmCfg<BN>;
     constexpr int STAGES = C::STAGES;
@@ -86,9 +93,10 @@ __global__ void __launch_bounds__(320, 1)
     uint8_t *sStage = smem + STAGES * C::STAGE_BYTES;
     uint64_t *full = (uint64_t *)(sStage + C::STAGING);
     uint64_t *empty = full + STAGES;
+    constexpr int TBUF = C::TBUF;
     uint64_t *tfull = empty + STAGES;
-    uint64_t *tempty = tfull + 2;
-    uint32_t *tslot = (uint32_t *)(tempty + 2);
+    uint64_t *tempty = tfull + TBUF;
+    uint32_t *tslot = (uint32_t *)(tempty + TBUF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -96,13 +104,14 @@ __global__ void __launch_bounds__(320, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < TBUF; b++) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 8);
         }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tslot, 512);
@@ -121,7 +130,7 @@ __global__ void __launch_bounds__(320, 1)
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                const int mb = t % g.m_tiles, nb = t / g.m_tiles;
+                const int nb = t % g.n_tiles, mb = t / g.n_tiles;  // N fastest: an A tile is read by neighbours
                 for (int k = 0; k < KI; k++) {
                     if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
@@ -157,8 +166,10 @@ __global__ void __launch_bounds__(320, 1)
                     umma_commit(&empty[stage]);
                     if (PROMOTE || k == KI - 1) {
                         umma_commit(&tfull[tb]);
-                        tb ^= 1;
-                        if (!tb) tph ^= 1;
+                        if (++tb == TBUF) {
+                            tb = 0;
+                            tph ^= 1;
+                        }
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -174,45 +185,55 @@ __global__ void __launch_bounds__(320, 1)
         EpiCtx cx;
         cx.lane = lane;
         cx.stage = sStage + ew * 4096;
+        cx.tmC = &tmC;
         uint32_t tb = 0, tph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-            const int mb = t % g.m_tiles, nb = t / g.m_tiles;
+            const int nb = t % g.n_tiles, mb = t / g.n_tiles;  // N fastest: an A tile is read by neighbours
             cx.row0 = mb * 128 + quad * 32;
             cx.col0 = nb * BN + half * COLS;
+            typename Epi::State es;
+            Epi::begin(ep, cx, es);  // per-tile loads issued before the accumulator is ready
             float2 acc[COLS / 2];
 #pragma unroll
             for (int j = 0; j < COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);
             const int units = PROMOTE ? KI : 1;
             const float *wsr = nullptr;
             if (PROMOTE) wsr = g.ws + (size_t)min(WS_ON_M ? mb : (cx.col0 >> 7), g.ws_rows - 1) * g.ws_ld;
+            float snext = PROMOTE ? __ldg(wsr) : 1.0f;
             for (int u = 0; u < units; u++) {
+                const float s = PROMOTE ? g.ascale * snext : 1.0f;
+                if (PROMOTE && u + 1 < units) snext = __ldg(wsr + u + 1);
                 // warp-uniform outcome: the tcgen05.ld below is a .sync.aligned warp instruction
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
                 tc_fence_after();
                 const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * BN + half * COLS;
-                const float s = PROMOTE ? g.ascale * __ldg(wsr + u) : 1.0f;
                 const float2 s2 = make_float2(s, s);
 #pragma unroll
-                for (int c = 0; c < COLS / 32; c++) {
-                    float v[32];
-                    tmem_ld32(taddr + c * 32, v);
+                for (int c = 0; c < COLS / 16; c++) {
+                    float v[16];
+                    tmem_ld16(taddr + c * 16, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        if (PROMOTE) acc[c * 16 + j] = ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[c * 16 + j]);
-                        else acc[c * 16 + j] = make_float2(v[2 * j], v[2 * j + 1]);
+                    for (int j = 0; j < 8; j++) {
+                        const float2 vv = make_float2(v[2 * j], v[2 * j + 1]);
+                        if (PROMOTE) acc[c * 8 + j] = ffma2(s2, vv, acc[c * 8 + j]);
+                        else acc[c * 8 + j] = vv;
                     }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[tb]);
-                tb ^= 1;
-                if (!tb) tph ^= 1;
+                if (++tb == TBUF) {
+                    tb = 0;
+                    tph ^= 1;
+                }
             }
             if (!ok) break;
-            Epi::apply(ep, (float *)acc, cx);
+            Epi::apply(ep, (float *)acc, cx, es);
         }
+        if (lane == 0) bulk_wait0();  // the epilogue's TMA stores / reductions have completed
+        __syncwarp();
     }
     __syncthreads();
     if (warp == 1) {
@@ -234,7 +255,9 @@ struct EpiF32 {
         float *out;
         int ld, M, N;
     };
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx)
+    using State = NoState;
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
 #pragma unroll
         for (int c = 0; c < COLS / 32; c++) {

@@ -16,8 +16,8 @@ static void load_encode()
         g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
 }
 
-int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t box_cols,
-                 uint32_t box_rows, CUtensorMapSwizzle swz)
+int make_tmap_2d_typed(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+                       uint64_t pitch, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz)
 {
     std::call_once(g_encode_once, load_encode);
     if (!g_encode) {
@@ -32,15 +32,20 @@ int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows,
     cuuint64_t strides[1] = {pitch};
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = g_encode(m, dt, 2, (void *)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         fprintf(stderr, "eva: cuTensorMapEncodeTiled failed (%d): cols %llu rows %llu pitch %llu box %ux%u\n", (int)r,
                 (unsigned long long)cols, (unsigned long long)rows, (unsigned long long)pitch, box_cols, box_rows);
         return -1;
     }
     return 0;
+}
+
+int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t box_cols,
+                 uint32_t box_rows, CUtensorMapSwizzle swz)
+{
+    return make_tmap_2d_typed(m, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, cols, rows, pitch, box_cols, box_rows, swz);
 }
 
 int num_sms(int device)

@@ -21,6 +21,9 @@ namespace xtb {
 // box_cols bytes x box_rows rows with the given swizzle. Out-of-range boxes read as zero.
 int make_tmap_2d(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t box_cols,
                  uint32_t box_rows, CUtensorMapSwizzle swz);
+// Same for elements of another type: cols / box_cols in elements, pitch in bytes.
+int make_tmap_2d_typed(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t cols, uint64_t rows,
+                       uint64_t pitch, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz);
 
 int num_sms(int device);
 

@@ -43,7 +43,7 @@ static int set_smem(const void *kern, size_t bytes)
 // One launch of the tcgen05 GEMM: A = a (M rows), B = b (N rows), K slices of 128 bytes.
 template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
 static int run_gemm(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
-                    const typename Epi::Params &ep, cudaStream_t st)
+                    const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr)
 {
     using Cfg = GemmCfg<BN>;
     auto kern = k_gemm<Epi, BN, F16, PROMOTE, WS_ON_M>;
@@ -67,7 +67,7 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, b.map, g, ep);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, b.map, tmc ? *tmc : a.map, g, ep);
     XTB_CK(cudaGetLastError());
     return 0;
 }
@@ -118,24 +118,39 @@ int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo
     return 0;
 }
 
+// The fp16 residual x [rows][1024] as the target of TMA reduce-adds: boxes of 64 halves x 32 rows, 128B swizzle.
+static int resid_map(CUtensorMap *m, __half *x, int rows)
+{
+    return make_tmap_2d_typed(m, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, (uint64_t)rows, D * 2, 64, 32,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 int launch_oproj(const Operand &a, const Weight8 &w, float ascale, int rows, __half *x, cudaStream_t st)
 {
-    EpiResid::Params p{x, rows};
-    return run_gemm<EpiResid, 256, false, true, false>(a, w.op, rows, D, w.ws, kb(w.k), kb(w.n), ascale, p, st);
+    CUtensorMap xm;
+    if (resid_map(&xm, x, rows)) return -1;
+    EpiResid::Params p{rows};
+    return run_gemm<EpiResid, 256, false, true, false>(a, w.op, rows, D, w.ws, kb(w.k), kb(w.n), ascale, p, st, &xm);
 }
 
 int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
                cudaStream_t st)
 {
-    EpiFC1::Params p{h8, stat, rs, rows};
-    return run_gemm<EpiFC1, 256, false, true, false>(h, w.op, rows, N12, w.ws, kb(w.k), kb(w.n), ascale, p, st);
+    CUtensorMap hm;  // h8 [rows][2736] E4M3, stored in boxes of 64 units x 32 rows (64B swizzle)
+    if (make_tmap_2d(&hm, h8, HIDP, (uint64_t)rows, HIDP, 64, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
+    EpiFC1::Params p{stat, rs, rows};
+    return run_gemm<EpiFC1, 256, false, true, false>(h, w.op, rows, N12, w.ws, kb(w.k), kb(w.n), ascale, p, st, &hm);
 }
 
-int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, const float2 *stat, const float *c,
+int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
                const float *d, cudaStream_t st)
 {
-    EpiFC2::Params p{x, stat, c, d, rows};
-    return run_gemm<EpiFC2, 256, false, true, false>(h8, w.op, rows, D, w.ws, kb(w.k), kb(w.n), ascale, p, st);
+    CUtensorMap xm;
+    if (resid_map(&xm, x, rows)) return -1;
+    k_rowstat<<<(rows + 255) / 256, 256, 0, st>>>(stat, rows);
+    XTB_CK(cudaGetLastError());
+    EpiFC2::Params p{stat, c, d, rows};
+    return run_gemm<EpiFC2, 256, false, true, false>(h8, w.op, rows, D, w.ws, kb(w.k), kb(w.n), ascale, p, st, &xm);
 }
 
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,

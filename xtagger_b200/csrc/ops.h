@@ -45,8 +45,9 @@ int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo
 int launch_oproj(const Operand &a, const Weight8 &w, float ascale, int rows, __half *x, cudaStream_t st);
 int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
                cudaStream_t st);
-int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, const float2 *stat,
-               const float *c, const float *d, cudaStream_t st);
+// stat: fc1's [NSTAT][rows] partials; consumed (row (mean, rstd) written into partial 0) before the GEMM.
+int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
+               const float *d, cudaStream_t st);
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
                    float qs_head, cudaStream_t st);
 int launch_head_f16(const Operand &hw, const Operand &pn, int nimg, int nt, const float *hb, float *out,

@@ -59,6 +59,25 @@ __global__ void __launch_bounds__(256) k_ln_e4m3(const __half *__restrict__ x, c
     }
 }
 
+// Row statistics of the SwiGLU output for the folded MLP LayerNorm: the NSTAT partials (sum u, sum u^2) that fc1
+// wrote for a row are added in a fixed order (bit-identical run to run, as eva_kernels.cu:205-210) and turned into
+// (mean, rstd) over the 2730 units (eps 1e-6, k_fc2's formula, eva_kernels.cu:318-320), written in place into
+// partial 0 of the row.
+__global__ void __launch_bounds__(256) k_rowstat(float2 *__restrict__ stat, int rows)
+{
+    const int row = blockIdx.x * 256 + threadIdx.x;
+    if (row >= rows) return;
+    float s = 0.f, q = 0.f;
+#pragma unroll 4
+    for (int g = 0; g < NSTAT; g++) {
+        const float2 v = stat[(size_t)g * rows + row];
+        s += v.x;
+        q += v.y;
+    }
+    const float mean = s * (1.0f / HID);
+    stat[row] = make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
+}
+
 // Mean over patch tokens 1..1024 of each image: x [img][1025][1024] fp16 -> pool [img][1024] fp32.
 // Grid (img, 16): 64 columns per block; thread (c, grp) sums 4 columns over a 64-token group; the 16 group
 // partials are added in a fixed order. Replaces k_pool (eva_kernels.cu:404-431).
