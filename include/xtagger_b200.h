@@ -109,13 +109,13 @@ int xtb_gemm_e4m3_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, c
 /* LayerNorm over 1024 (eps 1e-6) * g + b, * qs, E4M3: x fp16 [rows][1024] -> y [rows][1024]. Replaces k_ln
  * (kern_common.cuh:147-186). */
 int xtb_ln_e4m3(const uint16_t *x, const float *g, const float *b, uint8_t *y, int rows, float qs, void *stream);
-/* QKV projection with its attention-layout epilogue; rows = images * 1025. q8 / k8 [img][16][1152][64],
- * vt8 [img][16][64][1152] (pads must be zero). Replaces k_qkv (eva_kernels.cu:41-114). */
+/* QKV projection with its attention-layout epilogue; rows = images * 1025. q8 / k8 / v8 [img][16][1152][64]
+ * (rows t >= 1025 must be zero). Replaces k_qkv (eva_kernels.cu:41-114). */
 int xtb_qkv(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *q8, uint8_t *k8,
-            uint8_t *vt8, const float *cs, float cq, float ck, float cv, void *stream);
+            uint8_t *v8, const float *cs, float cq, float ck, float cv, void *stream);
 /* FP8 attention: out E4M3 [img * 1025][1024] (head h at column 64 h). Replaces k_flash / flash8
  * (eva_kernels.cu:116-122, kern_common.cuh:403-543). */
-int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, uint8_t *out, float sinv, float vo,
+int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg, uint8_t *out, float sinv, float vo,
                   void *stream);
 /* x fp16 [rows][1024] += ascale * a . Wo^T (block-scaled). Replaces k_oproj (eva_kernels.cu:134-162). */
 int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, void *stream);

@@ -188,10 +188,10 @@ void or_ln_e4m3(const uint16_t *x, const float *g, const float *b, int rows, flo
  * QKV epilogue (k_qkv, eva_kernels.cu:60-113): acc is the dequantised projection [rows][3072] (q | k | v).
  * q, k: * cq / ck, then for patch tokens (t >= 1) rotate pair (2j, 2j+1) of each head by angle j of
  * cs[t - 1][j] = (cos, sin); E4M3. v: * cv, E4M3. Layouts of this library's attention (the reference permutes head
- * dims for its mma.sync fragments instead): q8 / k8 [img][16][TP][64], vt8 [img][16][64][TP]; pads untouched.
+ * dims and transposes V for its mma.sync fragments instead): q8 / k8 / v8 [img][16][TP][64]; pads untouched.
  * ------------------------------------------------------------------------------------------------------------- */
 void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, float ck, float cv, uint8_t *q8,
-                     uint8_t *k8, uint8_t *vt8)
+                     uint8_t *k8, uint8_t *v8)
 {
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < rows; r++) {
@@ -216,7 +216,7 @@ void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, floa
         }
         for (int h = 0; h < OR_NH; h++)
             for (int d = 0; d < 64; d++)
-                vt8[(((size_t)b * OR_NH + h) * 64 + d) * OR_TP + t] = or_e4m3(a[2 * OR_D + h * 64 + d] * cv);
+                v8[(((size_t)b * OR_NH + h) * OR_TP + t) * 64 + d] = or_e4m3(a[2 * OR_D + h * 64 + d] * cv);
     }
 }
 
@@ -229,7 +229,7 @@ void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, floa
  *   out = fp16(O * vo / l) -> E4M3 (the reference stages the output as fp16, kern_common.cuh:527-541).
  * The reference takes the rescale decision per 16-row warp slice; this library's kernel per row, as here.
  * ------------------------------------------------------------------------------------------------------------- */
-void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, float sinv, float vo,
+void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg, float sinv, float vo,
                   int key_tile, uint8_t *out)
 {
     float lut[256];
@@ -243,7 +243,7 @@ void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int 
             for (int t = 0; t < OR_T; t++)
                 for (int d = 0; d < 64; d++) {
                     K[t * 64 + d] = lut[k8[(bh * OR_TP + t) * 64 + d]];
-                    V[t * 64 + d] = lut[vt8[(bh * 64 + d) * OR_TP + t]];
+                    V[t * 64 + d] = lut[v8[(bh * OR_TP + t) * 64 + d]];
                 }
             for (int qi = 0; qi < OR_T; qi++) {
                 float q[64], o[64];
@@ -555,7 +555,7 @@ int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, fl
     uint8_t *h = malloc((size_t)rows * OR_D);
     float *acc = malloc((size_t)rows * OR_N12 * 4);
     uint8_t *q8 = calloc((size_t)nimg * OR_NH * OR_TP * 64, 1), *k8 = calloc((size_t)nimg * OR_NH * OR_TP * 64, 1);
-    uint8_t *vt8 = calloc((size_t)nimg * OR_NH * OR_TP * 64, 1);
+    uint8_t *v8 = calloc((size_t)nimg * OR_NH * OR_TP * 64, 1);
     uint8_t *h8 = malloc((size_t)rows * OR_HIDP);
     double *rsum = malloc((size_t)rows * 8), *rsq = malloc((size_t)rows * 8);
     or_patch_embed(in, nimg, M.pe, M.pos, x);
@@ -563,8 +563,8 @@ int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, fl
         or_layer *L = &M.L[i];
         or_ln_e4m3(x, L->ln1w, L->ln1b, rows, 1.0f / L->adq[0], h);
         or_gemm_e4m3(h, rows, OR_D, L->wqkv, 3 * OR_D, L->sqkv, L->adq[0], acc);
-        or_qkv_epilogue(acc, rows, M.cs, L->cq, L->ck, L->cv, q8, k8, vt8);
-        or_attention(q8, k8, vt8, nimg, L->sinv, L->vo, key_tile, h);
+        or_qkv_epilogue(acc, rows, M.cs, L->cq, L->ck, L->cv, q8, k8, v8);
+        or_attention(q8, k8, v8, nimg, L->sinv, L->vo, key_tile, h);
         or_gemm_e4m3(h, rows, OR_D, L->wo, OR_D, L->so, L->adq[1], acc);
         or_resid_add(x, acc, rows);
         or_ln_e4m3(x, L->ln2w, L->ln2b, rows, 1.0f / L->adq[2], h);
@@ -588,7 +588,7 @@ int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, fl
     free(acc);
     free(q8);
     free(k8);
-    free(vt8);
+    free(v8);
     free(h8);
     free(rsum);
     free(rsq);

@@ -39,8 +39,8 @@ void or_gemm_f16(const uint16_t *a, int m, int k, const uint16_t *w, int n, floa
 /* forward pieces */
 void or_ln_e4m3(const uint16_t *x, const float *g, const float *b, int rows, float qs, uint8_t *y);
 void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, float ck, float cv, uint8_t *q8,
-                     uint8_t *k8, uint8_t *vt8);
-void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, float sinv, float vo,
+                     uint8_t *k8, uint8_t *v8);
+void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg, float sinv, float vo,
                   int key_tile, uint8_t *out);
 void or_resid_add(uint16_t *x, const float *acc, int rows);
 void or_fc1_epilogue(const float *acc, int rows, const float *rs, uint8_t *h8, double *rowsum, double *rowsq);

@@ -88,7 +88,7 @@ def test_teacher_forced_layers(xlib, cuda, models):
         lib.or_ln_e4m3(xh, c(L["ln1w"]), c(L["ln1b"]), rows, float(1 / L["adq"][0]), w)
         G.assert_e4m3_close(G.host(h), w, 1, 0.999, f"L{i} ln1")
         hh = G.host(h).copy()
-        shp, shv = (nimg, 16, 1152, 64), (nimg, 16, 64, 1152)
+        shp, shv = (nimg, 16, 1152, 64), (nimg, 16, 1152, 64)
         q8, k8, vt8 = G.zeros(shp, torch.uint8), G.zeros(shp, torch.uint8), G.zeros(shv, torch.uint8)
         assert xlib.xtb_qkv(G.P(h), rows, G.P(G.dev(L["qkv"])), G.P(G.dev(L["qkv_s"])), float(L["adq"][0]), G.P(q8),
                             G.P(k8), G.P(vt8), G.P(G.dev(cs)), float(L["cq"]), float(L["ck"]), float(L["cv"]), None) == 0

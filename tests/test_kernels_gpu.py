@@ -57,7 +57,7 @@ def test_qkv_epilogue_layouts(xlib, cuda, O):
     cs = M.rope_table()
     acc = O.gemm_e4m3(h, w, ws, adq)
     qw = np.zeros((NIMG, 16, TP, 64), np.uint8)
-    kw, vw = np.zeros_like(qw), np.zeros((NIMG, 16, 64, TP), np.uint8)
+    kw, vw = np.zeros_like(qw), np.zeros((NIMG, 16, TP, 64), np.uint8)
     O.lib().or_qkv_epilogue(acc, ROWS, cs, cq, ck, cv, qw, kw, vw)
     q8, k8, vt8 = (G.zeros(a.shape, torch.uint8) for a in (qw, kw, vw))
     rc = xlib.xtb_qkv(G.P(G.dev(h)), ROWS, G.P(G.dev(w)), G.P(G.dev(ws)), adq, G.P(q8), G.P(k8), G.P(vt8),
@@ -68,7 +68,7 @@ def test_qkv_epilogue_layouts(xlib, cuda, O):
         got = G.host(got)
         G.assert_e4m3_close(got, want, 1, 0.99, name)
     # padded key rows / columns untouched (zero)
-    assert not G.host(q8)[:, :, 1025:].any() and not G.host(vt8)[:, :, :, 1025:].any()
+    assert not G.host(q8)[:, :, 1025:].any() and not G.host(vt8)[:, :, 1025:].any()
 
 
 @pytest.mark.parametrize("peaked", [False, True])
@@ -79,10 +79,10 @@ def test_attention(xlib, cuda, O, peaked):
     sd = 3.0 if peaked else 1.0   # peaked: large scores, so lazy rescales and dead tiles occur
     q = np.zeros(shape, np.uint8)
     k = np.zeros(shape, np.uint8)
-    vt = np.zeros((NIMG, 16, 64, TP), np.uint8)
+    vt = np.zeros((NIMG, 16, TP, 64), np.uint8)
     q[:, :, :1025] = O.e4m3(rng.standard_normal((NIMG, 16, 1025, 64), dtype=np.float32) * 60 * sd)
     k[:, :, :1025] = O.e4m3(rng.standard_normal((NIMG, 16, 1025, 64), dtype=np.float32) * 60 * sd)
-    vt[:, :, :, :1025] = O.e4m3(rng.standard_normal((NIMG, 16, 64, 1025), dtype=np.float32) * 100)
+    vt[:, :, :1025] = O.e4m3(rng.standard_normal((NIMG, 16, 1025, 64), dtype=np.float32) * 100)
     sinv = (0.8 / 448) * (4.0 / 448)
     vo = (448 / 3.0) * (3.0 / 448) * 0.9
     want = np.empty((ROWS, D), np.uint8)

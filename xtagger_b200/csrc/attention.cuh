@@ -9,11 +9,12 @@
 //   - P is quantised to E4M3 for the P V product; l sums the unquantised p; out = O * vo / l -> E4M3.
 // Decisions are per query row here (one row per thread), where the reference takes them per 16-row warp slice.
 //
-// Warp roles (192 threads, 2 CTAs per SM): warp 0 TMA (Q once; K / V^T tiles through a 3-deep ring), warp 1 TMEM
+// Warp roles (192 threads, 2 CTAs per SM): warp 0 TMA (Q once; K / V tiles through a 3-deep ring), warp 1 TMEM
 // allocation (256 columns: S at [0,128), O at [128,192)) and the MMA issuer, warps 2..5 softmax, one row each.
 // S_j = Q K_j^T (M 128, N 128 keys, K 64 dims) -> TMEM; softmax reads it (two passes: max, then exp2 / quantise),
 // writes P_j (128 x 128 E4M3, 128B-swizzled K-major) to shared memory; O += P_j V_j (M 128, N 64 dims, K 128 keys)
-// accumulates in TMEM. S_{j+1} is issued as soon as the softmax has read S_j, ahead of PV_j.
+// accumulates in TMEM, with V read as an MN-major operand straight from its [token][64 dims] rows (64B swizzle,
+// 8-key groups 512 bytes apart). S_{j+1} is issued as soon as the softmax has read S_j, ahead of PV_j.
 #pragma once
 #include "ops.h"
 #include "ptx.cuh"
@@ -22,12 +23,12 @@ namespace xtb {
 
 constexpr float ATT_RESCALE = 8.0f;
 constexpr float ATT_PSKIP = 10.0f;
-constexpr int ATT_KS = 3;                 // K / V^T ring depth
+constexpr int ATT_KS = 3;                 // K / V ring depth
 constexpr int ATT_NK = TP / 128;          // key tiles (9; the last holds 1 key)
 constexpr int ATT_THREADS = 192;
 constexpr int ATT_Q_BYTES = 128 * 64;
 constexpr int ATT_K_BYTES = 128 * 64;
-constexpr int ATT_V_BYTES = 64 * 128;
+constexpr int ATT_V_BYTES = 128 * 64;
 constexpr int ATT_P_BYTES = 128 * 128;
 constexpr size_t ATT_SMEM = 1024 + ATT_Q_BYTES + ATT_KS * (ATT_K_BYTES + ATT_V_BYTES) + 2 * ATT_P_BYTES + 256;
 
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                 if (!mbar_wait(&kv_empty[st], ph ^ 1, err, XTB_ERR_WAIT_ATTN)) break;
                 mbar_arrive_expect_tx(&kv_full[st], ATT_K_BYTES + ATT_V_BYTES);
                 tma_load_2d(sK + st * ATT_K_BYTES, &tk, &kv_full[st], 0, bh * TP + j * 128);
-                tma_load_2d(sV + st * ATT_V_BYTES, &tv, &kv_full[st], j * 128, bh * HD);
+                tma_load_2d(sV + st * ATT_V_BYTES, &tv, &kv_full[st], 0, bh * TP + j * 128);
                 if (++st == ATT_KS) {
                     st = 0;
                     ph ^= 1;
@@ -108,7 +109,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         }
     } else if (warp == 1) {
         if (elect_one()) {
-            constexpr uint32_t ID_S = idesc_m128(128), ID_PV = idesc_m128(64);
+            // PV: B = V, MN-major (bit 16): its N (dims) run contiguous within each key's 64-byte row
+            constexpr uint32_t ID_S = idesc_m128(128), ID_PV = idesc_m128(64) | (1u << 16);
             const uint32_t q0 = smem_u32(sQ);
             bool ok = mbar_wait(q_full, 0, err, XTB_ERR_WAIT_ATTN);
             int st = 0, pst = 0;
@@ -132,8 +134,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                     const uint32_t v0 = smem_u32(sV + pst * ATT_V_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        umma<false>(tO, sdesc(p0 + kk * 32, 1024, SWZ_128B), sdesc(v0 + kk * 32, 1024, SWZ_128B), ID_PV,
-                                    (jp > 0 || kk > 0));
+                        umma<false>(tO, sdesc(p0 + kk * 32, 1024, SWZ_128B), sdesc_mn(v0 + kk * 2048, 512, SWZ_64B),
+                                    ID_PV, (jp > 0 || kk > 0));
                     umma_commit(&pv_done[jp & 1]);
                     umma_commit(&kv_empty[pst]);
                     if (++pst == ATT_KS) pst = 0;
@@ -155,16 +157,26 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             const int nvalid = min(128, T - j * 128);
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, err, XTB_ERR_WAIT_ATTN)))) break;
             tc_fence_after();
-            // pass 1: tile max of this row (keys past the sequence masked)
+            // pass 1: tile max of this row (keys past the sequence masked; chunks wholly past it skipped)
             float tm = -INFINITY;
+            if (nvalid == 128) {
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                float v[32];
-                tmem_ld32(tS + lrow + c * 32, v);
-                tmem_wait_ld();
+                for (int c = 0; c < 4; c++) {
+                    float v[32];
+                    tmem_ld32(tS + lrow + c * 32, v);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (c * 32 + i < nvalid) tm = fmaxf(tm, v[i]);
+                    for (int i = 0; i < 32; i++) tm = fmaxf(tm, v[i]);
+                }
+            } else {
+                for (int c = 0; c * 32 < nvalid; c++) {
+                    float v[32];
+                    tmem_ld32(tS + lrow + c * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (c * 32 + i < nvalid) tm = fmaxf(tm, v[i]);
+                }
             }
             // lazy rescale, decided per row: refresh m only when the tile max grew past m + thr
             float sc = 1.0f;
@@ -204,23 +216,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 #pragma unroll
                 for (int c = 0; c < 8; c++) *(uint4 *)(prow + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
             } else {
-                // pass 2: p = exp2((s - m) sinv), l += p, P = E4M3(p)
-                const float nm = -m * sinv;
+                // pass 2: p = exp2((s - m) sinv), l += p, P = E4M3(p); a dead row of a live warp writes zeros
+                const float nm = dead ? -INFINITY : -m * sinv;
+                const float sv = dead ? 0.f : sinv;
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    float v[32];
-                    tmem_ld32(tS + lrow + c * 32, v);
-                    tmem_wait_ld();
                     uint32_t w[8];
+                    if (c * 32 < nvalid) {  // warp-uniform
+                        float v[32];
+                        tmem_ld32(tS + lrow + c * 32, v);
+                        tmem_wait_ld();
+                        float l2 = 0.f;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float pp[4];
+                        for (int i = 0; i < 32; i += 4) {
+                            float pp[4];
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            pp[e] = (!dead && c * 32 + i + e < nvalid) ? ex2(fmaf(v[i + e], sinv, nm)) : 0.f;
-                            l += pp[e];
+                            for (int e = 0; e < 4; e++) {
+                                pp[e] = (nvalid == 128 || c * 32 + i + e < nvalid) ? ex2(fmaf(v[i + e], sv, nm)) : 0.f;
+                                l2 += pp[e];
+                            }
+                            w[i >> 2] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
                         }
-                        w[i >> 2] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
+                        l += l2;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) w[i] = 0;
                     }
                     *(uint4 *)(prow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
                     *(uint4 *)(prow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);

@@ -54,19 +54,19 @@ int xtb_ln_e4m3(const uint16_t *x, const float *g, const float *b, uint8_t *y, i
 }
 
 int xtb_qkv(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *q8, uint8_t *k8,
-            uint8_t *vt8, const float *cs, float cq, float ck, float cv, void *stream)
+            uint8_t *v8, const float *cs, float cq, float ck, float cv, void *stream)
 {
     Operand A;
     Weight8 W;
     if (!rows_ok(rows, "xtb_qkv") || make_operand(&A, h, rows, D, 128) || weight(&W, w, 3 * D, D, ws)) return -1;
-    return launch_qkv(A, W, ascale, rows, q8, k8, vt8, cs, cq, ck, cv, S(stream));
+    return launch_qkv(A, W, ascale, rows, q8, k8, v8, cs, cq, ck, cv, S(stream));
 }
 
-int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg, uint8_t *out, float sinv, float vo,
+int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg, uint8_t *out, float sinv, float vo,
                   void *stream)
 {
     Attn a;
-    if (nimg <= 0 || make_attn(&a, q8, k8, vt8, nimg)) return -1;
+    if (nimg <= 0 || make_attn(&a, q8, k8, v8, nimg)) return -1;
     return launch_attention(a, nimg, out, sinv, vo, S(stream));
 }
 

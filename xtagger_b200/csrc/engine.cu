@@ -44,7 +44,7 @@ struct Replica {
     uint8_t *wts = nullptr;
     float *sexp = nullptr;         // v3: expanded per-tensor scales
     __half *in = nullptr, *x = nullptr, *pn = nullptr;
-    uint8_t *h = nullptr, *q8 = nullptr, *k8 = nullptr, *vt8 = nullptr, *h8 = nullptr, *pn8 = nullptr;
+    uint8_t *h = nullptr, *q8 = nullptr, *k8 = nullptr, *v8 = nullptr, *h8 = nullptr, *pn8 = nullptr;
     float2 *stat = nullptr;
     float *pool = nullptr, *out = nullptr;
     uint8_t *hw = nullptr;         // head weights used by the forward (a copy when there are extra rows)
@@ -267,7 +267,7 @@ int forward(Impl *im, Replica &r, eva *e, Prof *p)
         Layer &L = r.L[i];
         RCK(launch_ln_e4m3(r.x, L.ln1w, L.ln1b, r.h, rows, 1.0f / L.adq[0], st));
         RCK(record(p, st, P_LN1));
-        RCK(launch_qkv(r.op_h, L.w[0], L.adq[0], rows, r.q8, r.k8, r.vt8, r.cs, L.cq, L.ck, L.cv, st));
+        RCK(launch_qkv(r.op_h, L.w[0], L.adq[0], rows, r.q8, r.k8, r.v8, r.cs, L.cq, L.ck, L.cv, st));
         RCK(record(p, st, P_QKV));
         RCK(launch_attention(r.attn, nb, r.h, L.sinv, L.vo, st));
         RCK(record(p, st, P_ATTN));
@@ -333,10 +333,10 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     const size_t qkb = (size_t)nb * NH * TP * HD;
     ECK(cudaMalloc(&r.q8, qkb));
     ECK(cudaMalloc(&r.k8, qkb));
-    ECK(cudaMalloc(&r.vt8, qkb));
+    ECK(cudaMalloc(&r.v8, qkb));
     ECK(cudaMemsetAsync(r.q8, 0, qkb, r.st));   // padded key / query rows stay zero forever
     ECK(cudaMemsetAsync(r.k8, 0, qkb, r.st));
-    ECK(cudaMemsetAsync(r.vt8, 0, qkb, r.st));
+    ECK(cudaMemsetAsync(r.v8, 0, qkb, r.st));
     ECK(cudaMalloc(&r.h8, (size_t)rows * HIDP));
     ECK(cudaMalloc(&r.stat, (size_t)NSTAT * rows * sizeof(float2)));
     ECK(cudaMalloc(&r.pool, (size_t)nb * D * 4));
@@ -360,7 +360,7 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
         RCK(make_operand(&r.op_hw, r.hw, (int)nt, D * 2, 128));
         RCK(make_operand(&r.op_pn, r.pn, nb, D * 2, 64));
     }
-    RCK(make_attn(&r.attn, r.q8, r.k8, r.vt8, nb));
+    RCK(make_attn(&r.attn, r.q8, r.k8, r.v8, nb));
     for (int s = 0; s < EVA_NBUF; s++)
         ECK(cudaEventCreateWithFlags(&r.done[s], cudaEventDisableTiming | cudaEventBlockingSync));
     ECK(cudaStreamSynchronize(r.st));
@@ -712,7 +712,7 @@ void eva_close(eva *e)
         if (r.graph) cudaGraphExecDestroy(r.graph);
         for (int s = 0; s < EVA_NBUF; s++)
             if (r.done[s]) cudaEventDestroy(r.done[s]);
-        void *bufs[] = {r.in, r.x, r.h, r.q8, r.k8, r.vt8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp};
+        void *bufs[] = {r.in, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp};
         for (void *p : bufs)
             if (p) cudaFree(p);
         if (r.head_copy) {

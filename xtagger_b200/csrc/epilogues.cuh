@@ -18,12 +18,11 @@ namespace xtb {
 
 // ---- QKV projection: acc = x W_qkv^T (dequantised); columns [0,1024) q, [1024,2048) k, [2048,3072) v ----
 // q, k: scaled by cq / ck, interleaved RoPE (pair (2j, 2j+1) of a head shares angle j, table cs[t - 1][j] =
-// (cos, sin)) for patch tokens t >= 1, E4M3 -> q8 / k8 [img][head][TP][64] (row t of 64 dims).
-// v: scaled by cv, E4M3 -> vt8 [img][head][64 dims][TP] (V transposed: keys contiguous per dim).
-// Padded key rows / columns t >= 1025 are zeroed once at allocation and never written.
+// (cos, sin)) for patch tokens t >= 1; v: scaled by cv. E4M3 -> q8 / k8 / v8 [img][head][TP][64] (row t of 64
+// dims; the attention reads V as an MN-major operand, so no transpose). Rows t >= 1025 stay zero.
 struct EpiQKV {
     struct Params {
-        uint8_t *q8, *k8, *vt8;
+        uint8_t *q8, *k8, *v8;
         const float2 *cs;
         float cq, ck, cv;
         int M;
@@ -35,60 +34,47 @@ struct EpiQKV {
         const int which = cx.col0 >> 10;           // 0 q, 1 k, 2 v (a thread's 128 columns never straddle)
         const int head0 = (cx.col0 & 1023) >> 6;   // two heads per thread
         const int row = cx.row0 + cx.lane;
-        const int b = row / T, t = row - b * T;
-        if (which < 2) {
-            const float sc = which ? p.ck : p.cq;
+        const int t = row % T;
+        const bool rope = which < 2 && t > 0 && row < p.M;
+        const float sc = which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
+        const float4 *cs4 = (const float4 *)(p.cs + (size_t)(rope ? t - 1 : 0) * 32);
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {          // 8 rotary pairs (16 dims) of both heads per step
+            float4 a[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) a[e] = rope ? __ldg(cs4 + (j >> 1) + e) : make_float4(1.f, 0.f, 1.f, 0.f);
 #pragma unroll
             for (int hh = 0; hh < 2; hh++) {
-                uint32_t w[16];
+                uint32_t w[4];
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
+                for (int e = 0; e < 8; e += 2) {
                     float f[4];
 #pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        float f0 = acc[hh * 64 + 2 * (j + e)] * sc, f1 = acc[hh * 64 + 2 * (j + e) + 1] * sc;
-                        if (t > 0 && row < p.M) {
-                            const float2 a = p.cs[(t - 1) * 32 + j + e];
-                            const float g0 = f0 * a.x - f1 * a.y;
-                            f1 = f1 * a.x + f0 * a.y;
-                            f0 = g0;
-                        }
-                        f[2 * e] = f0;
-                        f[2 * e + 1] = f1;
+                    for (int u = 0; u < 2; u++) {
+                        const float cosv = u ? a[e >> 1].z : a[e >> 1].x, sinv = u ? a[e >> 1].w : a[e >> 1].y;
+                        const float f0 = acc[hh * 64 + 2 * (j + e + u)] * sc, f1 = acc[hh * 64 + 2 * (j + e + u) + 1] * sc;
+                        f[2 * u] = f0 * cosv - f1 * sinv;
+                        f[2 * u + 1] = f1 * cosv + f0 * sinv;
                     }
-                    w[j >> 1] = e4m3x2(f[0], f[1]) | (e4m3x2(f[2], f[3]) << 16);
+                    w[e >> 1] = e4m3x2(f[0], f[1]) | (e4m3x2(f[2], f[3]) << 16);
                 }
-#pragma unroll
-                for (int c = 0; c < 4; c++)
-                    *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + c) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-            }
-            __syncwarp();
-            uint8_t *dst = which ? p.k8 : p.q8;
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int pc = i * 32 + cx.lane;          // piece: head hh, row r, 16-byte chunk ch
-                const int hh = pc >> 7, r = (pc >> 2) & 31, ch = pc & 3;
-                const int rw = cx.row0 + r;
-                if (rw < p.M) {
-                    const int bb = rw / T, tt = rw - bb * T;
-                    *(uint4 *)(dst + (((size_t)(bb * NH + head0 + hh) * TP + tt) << 6) + ch * 16) =
-                        *(const uint4 *)stage_chunk(cx.stage, r, 4 * hh + ch);
-                }
-            }
-            __syncwarp();
-        } else if (row < p.M) {
-            // V^T: for each dim, the 32 lanes (consecutive tokens) write consecutive key bytes
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                uint8_t *col = p.vt8 + ((size_t)(b * NH + head0 + hh) * HD) * TP + t;
-#pragma unroll
-                for (int d = 0; d < 64; d += 2) {
-                    const uint32_t pr = e4m3x2(acc[hh * 64 + d] * p.cv, acc[hh * 64 + d + 1] * p.cv);
-                    col[(size_t)d * TP] = (uint8_t)pr;
-                    col[(size_t)(d + 1) * TP] = (uint8_t)(pr >> 8);
-                }
+                *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + (j >> 3)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
+        __syncwarp();
+        uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int pc = i * 32 + cx.lane;          // piece: head hh, row r, 16-byte chunk ch
+            const int hh = pc >> 7, r = (pc >> 2) & 31, ch = pc & 3;
+            const int rw = cx.row0 + r;
+            if (rw < p.M) {
+                const int bb = rw / T, tt = rw - bb * T;
+                *(uint4 *)(dst + (((size_t)(bb * NH + head0 + hh) * TP + tt) << 6) + ch * 16) =
+                    *(const uint4 *)stage_chunk(cx.stage, r, 4 * hh + ch);
+            }
+        }
+        __syncwarp();
     }
 };
 

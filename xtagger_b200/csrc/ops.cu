@@ -93,19 +93,19 @@ int launch_ln_e4m3(const __half *x, const float *g, const float *b, uint8_t *y, 
     return 0;
 }
 
-int launch_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *q8, uint8_t *k8, uint8_t *vt8,
+int launch_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *q8, uint8_t *k8, uint8_t *v8,
                const float *cs, float cq, float ck, float cv, cudaStream_t st)
 {
-    EpiQKV::Params p{q8, k8, vt8, (const float2 *)cs, cq, ck, cv, rows};
+    EpiQKV::Params p{q8, k8, v8, (const float2 *)cs, cq, ck, cv, rows};
     return run_gemm<EpiQKV, 256, false, true, false>(h, w.op, rows, 3 * D, w.ws, kb(w.k), kb(w.n), ascale, p, st);
 }
 
-int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *vt8, int nimg)
+int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg)
 {
     const uint64_t rows = (uint64_t)nimg * NH * TP;
     if (make_tmap_2d(&a->tq, q8, HD, rows, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     if (make_tmap_2d(&a->tk, k8, HD, rows, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
-    if (make_tmap_2d(&a->tv, vt8, TP, (uint64_t)nimg * NH * HD, TP, 128, HD, CU_TENSOR_MAP_SWIZZLE_128B)) return -1;
+    if (make_tmap_2d(&a->tv, v8, HD, rows, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     return 0;
 }
 

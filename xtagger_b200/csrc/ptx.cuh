@@ -228,6 +228,20 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t sbo_bytes, ui
 }
 constexpr uint32_t SWZ_128B = 2, SWZ_64B = 4;
 
+// Descriptor of an MN-major operand tile (rows along K, each row a 64-byte run of MN elements, 64B swizzle): SBO =
+// byte distance between 8-row groups along K; LBO (distance between 64-byte column groups along MN) is unused for
+// a tile no wider than one swizzle atom and set to the tile's own size.
+__device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t sbo_bytes, uint32_t swz)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((8192u >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)(swz & 7u) << 61;
+    return d;
+}
+
 // Instruction descriptor (kind::f8f6f4 with E4M3 operands, or kind::f16 with fp16 operands), fp32 accumulate,
 // both operands K-major, M = 128. Bits: [4,6) D format (1 = f32), [7,10) A format, [10,13) B format,
 // [15] A major, [16] B major, [17,23) N >> 3, [24,29) M >> 4.
