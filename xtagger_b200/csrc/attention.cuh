@@ -10,7 +10,10 @@
 // Decisions are per query row here (one row per thread), where the reference takes them per 16-row warp slice.
 //
 // Warp roles (192 threads, 2 CTAs per SM): warp 0 TMA (Q once; K / V tiles through a 3-deep ring), warp 1 TMEM
-// allocation (256 columns: S at [0,128), O at [128,192)) and the MMA issuer, warps 2..5 softmax, one row each.
+// allocation (256 columns: S at [0,128), O at [128,192)) and the MMA issuer, warps 2..5 softmax, one query row per
+// thread. After the first tile the softmax makes a single pass over S with the running max (p, l and P computed
+// while the tile max is tracked) and only re-passes a warp when one of its rows crossed the lazy-rescale
+// threshold; warps whose 32 query rows are all padding (the last query tile holds one real row) skip the math.
 // S_j = Q K_j^T (M 128, N 128 keys, K 64 dims) -> TMEM; softmax reads it (two passes: max, then exp2 / quantise),
 // writes P_j (128 x 128 E4M3, 128B-swizzled K-major) to shared memory; O += P_j V_j (M 128, N 64 dims, K 128 keys)
 // accumulates in TMEM, with V read as an MN-major operand straight from its [token][64 dims] rows (64B swizzle,
@@ -37,6 +40,82 @@ __device__ __forceinline__ float ex2(float x)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+__device__ __forceinline__ float2 ffma2_(float2 a, float2 b, float2 c)
+{
+    uint64_t d = *reinterpret_cast<uint64_t *>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+__device__ __forceinline__ float2 fadd2_(float2 a, float2 b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
+    return *reinterpret_cast<float2 *>(&d);
+}
+
+// Max of a row's valid scores in the S tile (TMEM, 128 columns at sS).
+__device__ __forceinline__ float tile_max(uint32_t sS, int nvalid)
+{
+    float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        if (c * 32 < nvalid) {  // warp-uniform
+            float v[32];
+            tmem_ld32(sS + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                if (nvalid == 128 || c * 32 + i < nvalid) t4[i & 3] = fmaxf(t4[i & 3], v[i]);
+        }
+    }
+    return fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
+}
+
+// One pass over a row of the S tile with max m: tile max, p = exp2((s - m) sinv), sum of p, E4M3(p) -> the row of P
+// (128B-swizzled). Masked keys give p = 0.
+__device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int nvalid, float2 sv2, float m, float *tm_out,
+                                         float *l_out)
+{
+    const float2 nm2 = make_float2(-m * sv2.x, -m * sv2.x);
+    float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        uint32_t w[8];
+        if (c * 32 < nvalid) {  // warp-uniform
+            float v[32];
+            tmem_ld32(sS + c * 32, v);
+            tmem_wait_ld();
+            if (nvalid < 128) {
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (c * 32 + i >= nvalid) v[i] = -INFINITY;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                float pp[4];
+#pragma unroll
+                for (int e = 0; e < 4; e += 2) {
+                    t4[e] = fmaxf(t4[e], v[i + e]);
+                    t4[e + 1] = fmaxf(t4[e + 1], v[i + e + 1]);
+                    const float2 a = ffma2_(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
+                    pp[e] = ex2(a.x);
+                    pp[e + 1] = ex2(a.y);
+                    l2[e >> 1] = fadd2_(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
+                }
+                w[i >> 2] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) w[i] = 0;
+        }
+        *(uint4 *)(prow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *(uint4 *)(prow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    *tm_out = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
+    *l_out = (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 2)
@@ -150,101 +229,69 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         const int quad = warp & 3;
         const int r = quad * 32 + lane;                 // query row within the tile = TMEM lane
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
+        const uint32_t sS = tS + lrow, sO = tO + lrow;
         const float thr = ATT_RESCALE / sinv, dthr = ATT_PSKIP / sinv;
+        const bool idle = qt * 128 + quad * 32 >= T;     // warp-uniform: every row of the warp is padding
+        const float2 sv2 = make_float2(sinv, sinv);
         float m = -1e30f, l = 0.f;
         bool ok = true;
         for (int j = 0; j < ATT_NK && ok; j++) {
             const int nvalid = min(128, T - j * 128);
+            uint8_t *prow = sP + (j & 1) * ATT_P_BYTES + r * 128;
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, err, XTB_ERR_WAIT_ATTN)))) break;
-            tc_fence_after();
-            // pass 1: tile max of this row (keys past the sequence masked; chunks wholly past it skipped)
-            float tm = -INFINITY;
-            if (nvalid == 128) {
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    float v[32];
-                    tmem_ld32(tS + lrow + c * 32, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) tm = fmaxf(tm, v[i]);
-                }
-            } else {
-                for (int c = 0; c * 32 < nvalid; c++) {
-                    float v[32];
-                    tmem_ld32(tS + lrow + c * 32, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (c * 32 + i < nvalid) tm = fmaxf(tm, v[i]);
-                }
-            }
-            // lazy rescale, decided per row: refresh m only when the tile max grew past m + thr
-            float sc = 1.0f;
-            const bool resc = tm > m + thr;
-            if (resc) {
-                sc = ex2((m - tm) * sinv);
-                l *= sc;
-                m = tm;
-            }
-            // O (P V of the earlier tiles) is rescaled in TMEM once PV_{j-1} has landed; TMEM access is
-            // warp-collective, so the warp does it when any of its rows needs it (factor 1 for the others)
-            if (j > 0 && __any_sync(0xffffffffu, resc)) {
-                const int jp = j - 1;
-                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[jp & 1], (jp >> 1) & 1, err, XTB_ERR_WAIT_ATTN))))
-                    break;
-                tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    float v[16];
-                    tmem_ld16(tO + lrow + c * 16, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; i++) v[i] *= sc;
-                    tmem_st16(tO + lrow + c * 16, v);
-                }
-                tmem_wait_st();
-            }
             // P buffer j & 1 was last read by PV_{j-2}
             if (j >= 2) {
                 const int jq = j - 2;
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[jq & 1], (jq >> 1) & 1, err, XTB_ERR_WAIT_ATTN))))
                     break;
             }
-            uint8_t *prow = sP + (j & 1) * ATT_P_BYTES + r * 128;
-            const bool dead = tm < m - dthr;   // every p of the row's tile rounds to zero in E4M3
-            if (__all_sync(0xffffffffu, dead)) {
+            tc_fence_after();
+            if (idle) {
 #pragma unroll
                 for (int c = 0; c < 8; c++) *(uint4 *)(prow + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
             } else {
-                // pass 2: p = exp2((s - m) sinv), l += p, P = E4M3(p); a dead row of a live warp writes zeros
-                const float nm = dead ? -INFINITY : -m * sinv;
-                const float sv = dead ? 0.f : sinv;
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    uint32_t w[8];
-                    if (c * 32 < nvalid) {  // warp-uniform
-                        float v[32];
-                        tmem_ld32(tS + lrow + c * 32, v);
-                        tmem_wait_ld();
-                        float l2 = 0.f;
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            float pp[4];
-#pragma unroll
-                            for (int e = 0; e < 4; e++) {
-                                pp[e] = (nvalid == 128 || c * 32 + i + e < nvalid) ? ex2(fmaf(v[i + e], sv, nm)) : 0.f;
-                                l2 += pp[e];
-                            }
-                            w[i >> 2] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
-                        }
-                        l += l2;
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 8; i++) w[i] = 0;
+                // one pass with the running max: tile max, p = exp2((s - m) sinv), l_tile, P
+                float tm = -INFINITY, lt = 0.f;
+                if (j > 0) exp_pass(sS, prow, r, nvalid, sv2, m, &tm, &lt);
+                else tm = tile_max(sS, nvalid);
+                const bool resc = tm > m + thr;
+                if (__any_sync(0xffffffffu, resc)) {
+                    float sc = 1.0f;
+                    if (resc) {
+                        sc = ex2((m - tm) * sinv);
+                        l *= sc;
+                        m = tm;
                     }
-                    *(uint4 *)(prow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *(uint4 *)(prow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+                    if (j > 0) {
+                        // O holds P V of the earlier tiles: rescale it in TMEM once PV_{j-1} has landed (TMEM
+                        // access is warp-collective: factor 1 for the rows that keep their max)
+                        const int jp = j - 1;
+                        if (!(ok = __all_sync(0xffffffffu,
+                                              mbar_wait(&pv_done[jp & 1], (jp >> 1) & 1, err, XTB_ERR_WAIT_ATTN))))
+                            break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            float v[16];
+                            tmem_ld16(sO + c * 16, v);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; i++) v[i] *= sc;
+                            tmem_st16(sO + c * 16, v);
+                        }
+                        tmem_wait_st();
+                    }
+                    // (re)compute P with the refreshed max; rows that kept theirs recompute the same values
+                    float tm2, lt2;
+                    exp_pass(sS, prow, r, nvalid, sv2, m, &tm2, &lt2);
+                    lt = lt2;
                 }
+                if (tm < m - dthr) {   // dead row: every p of the tile rounds to zero in E4M3, l unchanged
+#pragma unroll
+                    for (int c = 0; c < 8; c++) *(uint4 *)(prow + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                    lt = 0.f;
+                }
+                l += lt;
             }
             // S_j fully read: the tensor core may overwrite it with S_{j+1}
             tc_fence_before();
@@ -259,14 +306,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             const int jl = ATT_NK - 1;
             ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[jl & 1], (jl >> 1) & 1, err, XTB_ERR_WAIT_ATTN));
         }
-        if (ok) {
+        if (ok && !idle) {
             tc_fence_after();
             const float f = vo / l;
             uint32_t w[16];
 #pragma unroll
             for (int c = 0; c < 2; c++) {
                 float v[32];
-                tmem_ld32(tO + lrow + c * 32, v);
+                tmem_ld32(sO + c * 32, v);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i += 4)
