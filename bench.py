@@ -157,18 +157,12 @@ def run_ours(args, rank, world, local):
         if pg:
             pg.barrier()
 
-    def allmax(v):
-        if not pg:
-            return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
-
+    from xtagger_b200.dist import allmax, shard_bounds
     model = model_path(rank, world, barrier)
-    nb = args.batch // world
-    assert nb * world == args.batch, "global batch must split evenly"
+    lo, hi = shard_bounds(args.batch, world, rank)
+    nb = hi - lo
     allx = M.synthetic_inputs(args.batch, seed=1)
-    pool = np.ascontiguousarray(allx[rank * nb:(rank + 1) * nb])
+    pool = np.ascontiguousarray(allx[lo:hi])
     eng = Engine(model, devices=(local,), nb=nb, pool=pool)
     eng.ready()
     st = torch.cuda.ExternalStream(eng.stream(0), device=torch.device("cuda", local))
@@ -234,7 +228,7 @@ def run_ours(args, rank, world, local):
                 "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
                 "config": {"workload": "config 3: EVA02-L 448^2 forward (24 layers, d 1024, 1025 tokens, 10861-tag "
                                        "FP8 head), global batch split across the GPUs",
-                           "global_batch": args.batch, "per_gpu_batch": nb, "parallelism": f"dp{world}",
+                           "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
                            "weights": "random-init, E4M3 with fp32 scales per 128x128 block",
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
                 "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": args.batch * 1024 * 592 * 2,
