@@ -140,6 +140,17 @@ int xtb_head_f16(const uint16_t *hw, int nt, const uint16_t *pn, int nimg, const
 int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *pn8, int nimg, float ascale,
                   const float *hb, float *out, void *stream);
 
+/* fc2 as xtb_fc2, allocating nothing: its scratch (per-row mean / rstd, bounded-wait status) lives in a static
+ * device array of the library, sized for XTB_NOALLOC_MAX_ROWS rows. No counterpart in the reference. For callers
+ * that cannot let the library allocate device memory (their own fixed memory arena, no cudaMalloc
+ * synchronisation on a latency-critical path, no out-of-memory failure after start-up). `stat` (fc1's partials)
+ * is only read. Rows beyond the maximum are rejected (-1). The first call on a device sets up the array's address
+ * and should come before any stream capture. All calls on a device share the array: calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+#define XTB_NOALLOC_MAX_ROWS (16 * 1025)
+int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x,
+                    const float *stat, const float *c, const float *d, void *stream);
+
 /* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). */
 uint32_t xtb_error_word(int device);
 void xtb_error_clear(int device);

@@ -1,0 +1,136 @@
+// fc2 (with the folded MLP LayerNorm) without any device allocation.
+//
+// Some callers cannot let a library allocate device memory: a host application that hands out all GPU memory
+// from its own fixed arena and accounts for every byte, a caller on a latency-critical path that cannot afford
+// cudaMalloc's implicit device-wide synchronisation, or one that must not fail on an out-of-memory at run time
+// after start-up. xtb_fc2 needs two pieces of device scratch beyond its inputs and outputs -- the per-row
+// (mean, rstd) of the SwiGLU output and the word in which kernels record a bounded wait that ran out -- and the
+// library allocates the latter with cudaMalloc on first use. xtb_fc2_noalloc keeps both in one file-scope static
+// device array of fixed size instead, and leaves the caller's fc1 partials untouched.
+//
+// Limits and sharing: at most XTB_NOALLOC_MAX_ROWS rows (16 images of 1025 tokens; 131 KB of row statistics).
+// Every GPU that loads the library holds the array until the process exits. All calls on a device share it and it
+// keeps the last call's contents: the row statistics are fully rewritten by every call and the status word is
+// cleared at the start of every call. Calls whose work overlaps on the GPU (different streams, or host threads
+// racing on one device) race on the array and must be serialised by the caller.
+//
+// Set-up: the first call on a device, with that device current, looks up the array's device address
+// (cudaGetSymbolAddress) and sets the GEMM kernel's shared-memory attribute; that first call should come before
+// any stream capture.
+#include <mutex>
+
+#include "../../include/xtagger_b200.h"
+#include "epilogues.cuh"
+#include "gemm.cuh"
+#include "host.h"
+#include "ops.h"
+
+using namespace xtb;
+
+namespace {
+
+struct NoAllocScratch {
+    uint32_t status[64];                      // bounded-wait failures of the last call (256 bytes)
+    float2 ms[XTB_NOALLOC_MAX_ROWS];          // per-row (mean, rstd) over the 2730 SwiGLU units
+};
+
+// In host code this name is only a stand-in for the device object: host code uses the address returned by
+// cudaGetSymbolAddress for the current device, never the name itself.
+static __device__ __align__(256) NoAllocScratch g_noalloc;
+
+// (mean, rstd) of every row from fc1's NSTAT partials, summed in a fixed order (as k_rowstat), into ms.
+__global__ void __launch_bounds__(256) k_rowstat_into(const float2 *__restrict__ stat, float2 *__restrict__ ms, int rows)
+{
+    const int row = blockIdx.x * 256 + threadIdx.x;
+    if (row >= rows) return;
+    float s = 0.f, q = 0.f;
+#pragma unroll 4
+    for (int g = 0; g < NSTAT; g++) {
+        const float2 v = stat[(size_t)g * rows + row];
+        s += v.x;
+        q += v.y;
+    }
+    const float mean = s * (1.0f / HID);
+    ms[row] = make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
+}
+
+using Fc2Kernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, EpiFC2::Params);
+
+struct DeviceScratch {
+    bool ready = false;
+    NoAllocScratch *ptr = nullptr;
+};
+std::mutex g_mu;
+DeviceScratch g_dev[64];
+
+// Once per device, with the device current: the array's device address and the GEMM's shared-memory opt-in.
+int setup(int dev, NoAllocScratch **out)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev < 0 || dev >= 64) {
+        fprintf(stderr, "eva: xtb_fc2_noalloc: device %d out of range\n", dev);
+        return -1;
+    }
+    DeviceScratch &d = g_dev[dev];
+    if (!d.ready) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc);
+        if (e != cudaSuccess || !p) {
+            fprintf(stderr, "eva: xtb_fc2_noalloc: cudaGetSymbolAddress: %s\n", cudaGetErrorString(e));
+            return -1;
+        }
+        const Fc2Kernel k = k_gemm<EpiFC2, 256, false, true, false>;
+        e = cudaFuncSetAttribute((const void *)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<256>::SMEM);
+        if (e != cudaSuccess) {
+            fprintf(stderr, "eva: xtb_fc2_noalloc: cudaFuncSetAttribute: %s\n", cudaGetErrorString(e));
+            return -1;
+        }
+        d.ptr = (NoAllocScratch *)p;
+        d.ready = true;
+    }
+    *out = d.ptr;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x,
+                               const float *stat, const float *c, const float *d, void *stream)
+{
+    if (rows <= 0 || rows > XTB_NOALLOC_MAX_ROWS) {
+        fprintf(stderr, "eva: xtb_fc2_noalloc: %d rows; the static scratch holds 1..%d rows (16 images)\n", rows,
+                XTB_NOALLOC_MAX_ROWS);
+        return -1;
+    }
+    int dev = 0;
+    XTB_CK(cudaGetDevice(&dev));
+    NoAllocScratch *sc = nullptr;
+    if (setup(dev, &sc)) return -1;
+    cudaStream_t st = (cudaStream_t)stream;
+    Operand A, B;
+    CUtensorMap xm;
+    if (make_operand(&A, h8, rows, HIDP, 128) || make_operand(&B, w, D, HIDP, 256) ||
+        make_tmap_2d_typed(&xm, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, (uint64_t)rows, D * 2, 64, 32,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+        return -1;
+    XTB_CK(cudaMemsetAsync(sc->status, 0, sizeof(sc->status), st));
+    k_rowstat_into<<<(rows + 255) / 256, 256, 0, st>>>((const float2 *)stat, sc->ms, rows);
+    XTB_CK(cudaGetLastError());
+    GemmArgs g;
+    g.M = rows;
+    g.N = D;
+    g.kiters = (HIDP + 127) / 128;
+    g.m_tiles = (rows + 127) / 128;
+    g.n_tiles = D / 256;
+    g.ws = ws;
+    g.ws_ld = (HIDP + 127) / 128;
+    g.ws_rows = D / 128;
+    g.ascale = ascale;
+    g.err = sc->status;
+    const int total = g.m_tiles * g.n_tiles;
+    const int grid = total < num_sms(dev) ? total : num_sms(dev);
+    EpiFC2::Params p{sc->ms, c, d, rows};
+    k_gemm<EpiFC2, 256, false, true, false><<<grid, GemmCfg<256>::THREADS, GemmCfg<256>::SMEM, st>>>(A.map, B.map, xm, g, p);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}

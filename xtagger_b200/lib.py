@@ -58,6 +58,7 @@ _SIGS = {
     "xtb_pool_ln": (C.c_int, [_P, C.c_int, _P, _P, _P, _P, _P, C.c_float, _P]),
     "xtb_head_f16": (C.c_int, [_P, C.c_int, _P, C.c_int, _P, _P, _P]),
     "xtb_head_e4m3": (C.c_int, [_P, C.c_int, _P, _P, C.c_int, C.c_float, _P, _P, _P]),
+    "xtb_fc2_noalloc": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
     "xtb_error_word": (C.c_uint32, [C.c_int]),
     "xtb_error_clear": (None, [C.c_int]),
 }
