@@ -42,19 +42,6 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
-__device__ __forceinline__ float2 ffma2_(float2 a, float2 b, float2 c)
-{
-    uint64_t d = *reinterpret_cast<uint64_t *>(&c);
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
-    return *reinterpret_cast<float2 *>(&d);
-}
-__device__ __forceinline__ float2 fadd2_(float2 a, float2 b)
-{
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(*reinterpret_cast<uint64_t *>(&a)), "l"(*reinterpret_cast<uint64_t *>(&b)));
-    return *reinterpret_cast<float2 *>(&d);
-}
-
 // Max of a row's valid scores in the S tile (TMEM, 128 columns at sS).
 __device__ __forceinline__ float tile_max(uint32_t sS, int nvalid)
 {
@@ -100,10 +87,10 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int 
                 for (int e = 0; e < 4; e += 2) {
                     t4[e] = fmaxf(t4[e], v[i + e]);
                     t4[e + 1] = fmaxf(t4[e + 1], v[i + e + 1]);
-                    const float2 a = ffma2_(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
+                    const float2 a = fma2(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
                     pp[e] = ex2(a.x);
                     pp[e + 1] = ex2(a.y);
-                    l2[e >> 1] = fadd2_(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
+                    l2[e >> 1] = add2(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
                 }
                 w[i >> 2] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
             }

@@ -28,7 +28,22 @@ struct EpiQKV {
         int M;
     };
     using State = NoState;
-    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    // cq / ck / cv ride along with the block-scale promotion, so acc arrives already scaled
+    __device__ __forceinline__ static float col_scale(const Params &p, const EpiCtx &cx)
+    {
+        const int which = cx.col0 >> 10;
+        return which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
+    }
+    // pull the row's RoPE angles (256 bytes) into L1 while the accumulator is being built
+    __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &)
+    {
+        const int row = cx.row0 + cx.lane, t = row % T;
+        if ((cx.col0 >> 10) < 2 && t > 0 && row < p.M) {
+            const char *a = (const char *)(p.cs + (size_t)(t - 1) * 32);
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(a + 128));
+        }
+    }
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
         const int which = cx.col0 >> 10;           // 0 q, 1 k, 2 v (a thread's 128 columns never straddle)
@@ -36,7 +51,6 @@ struct EpiQKV {
         const int row = cx.row0 + cx.lane;
         const int t = row % T;
         const bool rope = which < 2 && t > 0 && row < p.M;
-        const float sc = which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
         const float4 *cs4 = (const float4 *)(p.cs + (size_t)(rope ? t - 1 : 0) * 32);
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {          // 8 rotary pairs (16 dims) of both heads per step
@@ -48,15 +62,15 @@ struct EpiQKV {
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 8; e += 2) {
-                    float f[4];
+                    float2 f[2];
 #pragma unroll
                     for (int u = 0; u < 2; u++) {
+                        // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin) as two packed ops
                         const float cosv = u ? a[e >> 1].z : a[e >> 1].x, sinv = u ? a[e >> 1].w : a[e >> 1].y;
-                        const float f0 = acc[hh * 64 + 2 * (j + e + u)] * sc, f1 = acc[hh * 64 + 2 * (j + e + u) + 1] * sc;
-                        f[2 * u] = f0 * cosv - f1 * sinv;
-                        f[2 * u + 1] = f1 * cosv + f0 * sinv;
+                        const float f0 = acc[hh * 64 + 2 * (j + e + u)], f1 = acc[hh * 64 + 2 * (j + e + u) + 1];
+                        f[u] = fma2(make_float2(f1, f0), make_float2(-sinv, sinv), mul2(make_float2(f0, f1), make_float2(cosv, cosv)));
                     }
-                    w[e >> 1] = e4m3x2(f[0], f[1]) | (e4m3x2(f[2], f[3]) << 16);
+                    w[e >> 1] = e4m3x2(f[0].x, f[0].y) | (e4m3x2(f[1].x, f[1].y) << 16);
                 }
                 *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + (j >> 3)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
@@ -106,6 +120,7 @@ struct EpiResid {
         int M;
     };
     using State = NoState;
+    __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
@@ -125,12 +140,13 @@ struct EpiFC1 {
         int M;
     };
     using State = NoState;
+    __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
         const int row = cx.row0 + cx.lane;
         if (cx.col0 >= N12) return;  // warp-uniform: this half of the last tile is past the units
-        float s = 0.f, q = 0.f;
+        float2 s2 = make_float2(0.f, 0.f), q2 = make_float2(0.f, 0.f);
         if (cx.lane == 0) bulk_wait_read0();
         __syncwarp();
 #pragma unroll
@@ -143,21 +159,22 @@ struct EpiFC1 {
 #pragma unroll
             for (int i = 0; i < 16; i += 4) {
                 const float4 r4 = __ldg(rs4 + (i >> 2));
-                const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
-                float hq[4];
+                float2 hq[2];
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float gg = acc[32 * c + i + e], xx = acc[32 * c + 16 + i + e];
-                    const float u = xx * (0.5f * gg * (1.0f + tanh_fast(0.5f * gg)));
-                    s += u;
-                    q += u * u;
-                    hq[e] = u * rr[e];
+                for (int e = 0; e < 4; e += 2) {
+                    // u = x * (g/2) (1 + tanh(g/2)) on pairs of units
+                    const float2 hg = mul2(make_float2(acc[32 * c + i + e], acc[32 * c + i + e + 1]), make_float2(0.5f, 0.5f));
+                    const float2 th = make_float2(tanh_fast(hg.x), tanh_fast(hg.y));
+                    const float2 u = mul2(make_float2(acc[32 * c + 16 + i + e], acc[32 * c + 16 + i + e + 1]), fma2(hg, th, hg));
+                    s2 = add2(s2, u);
+                    q2 = fma2(u, u, q2);
+                    hq[e >> 1] = mul2(u, e ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y));
                 }
-                w[i >> 2] = e4m3x2(hq[0], hq[1]) | (e4m3x2(hq[2], hq[3]) << 16);
+                w[i >> 2] = e4m3x2(hq[0].x, hq[0].y) | (e4m3x2(hq[1].x, hq[1].y) << 16);
             }
             *(uint4 *)(cx.stage + cx.lane * 64 + ((c ^ ((cx.lane >> 1) & 3)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        if (row < p.M) p.stat[(size_t)(cx.col0 >> 7) * p.M + row] = make_float2(s, q);
+        if (row < p.M) p.stat[(size_t)(cx.col0 >> 7) * p.M + row] = make_float2(s2.x + s2.y, q2.x + q2.y);
         fence_proxy_async_smem();
         __syncwarp();
         if (cx.lane == 0 && cx.row0 < p.M) {
@@ -179,6 +196,7 @@ struct EpiFC2 {
     struct State {
         float2 ms;
     };
+    __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &st)
     {
         const int row = cx.row0 + cx.lane;
@@ -206,6 +224,7 @@ struct EpiPatch {
         int M;  // patch rows = images * 1024
     };
     using State = NoState;
+    __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
@@ -246,6 +265,7 @@ struct EpiHead {
         int nt, nimg;
     };
     using State = NoState;
+    __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {

@@ -30,17 +30,19 @@ struct GemmArgs {
     uint32_t *err;       // library error word
 };
 
-template <int BN>
+template <int BN, int EW = 8>
 struct GemmCfg {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
-    static constexpr int COLS = BN / 2;  // accumulator columns per epilogue thread
+    static constexpr int EPI_WARPS = EW;   // epilogue warps: EW / 4 per TMEM lane quadrant
+    static constexpr int COLS = BN / (EW / 4);  // accumulator columns per epilogue thread
     static constexpr int TBUF = 512 / BN;  // TMEM accumulator buffers (512 columns in all)
-    static constexpr int STAGING = 8 * 4096;
+    static constexpr int STAGE_PER_WARP = 32768 / EW;  // staging bytes per epilogue warp
+    static constexpr int STAGING = 32768;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + STAGING + 512;  // + barriers
-    static constexpr int THREADS = 320;
+    static constexpr int THREADS = 64 + 32 * EW;
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -75,14 +77,14 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
     return *reinterpret_cast<float2 *>(&d);
 }
 
-template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
-// 320 threads put three warps on two of the SM's four sub-partitions (16K registers each): at most 168
-// registers per thread.
-__global__ void __launch_bounds__(320, 1)
+// With 8 epilogue warps (320 threads) three warps share two of the SM's four sub-partitions (16K registers
+// each): at most 168 registers per thread; with 16 (576 threads) five share one: at most 96.
+template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M, int EW = 8>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
            const __grid_constant__ CUtensorMap tmC, const GemmArgs g, const typename Epi::Params ep)
 {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, EW>;
     constexpr int STAGES = C::STAGES;
     constexpr int COLS = C::COLS;
     constexpr uint32_t IDESC = idesc_m128(BN);
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         for (int b = 0; b < TBUF; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 8);
+            mbar_init(&tempty[b], EW);
         }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -181,10 +183,10 @@ __global__ void __launch_bounds__(320, 1)
     } else {
         const int ew = warp - 2;
         const int quad = warp & 3;
-        const int half = ew >> 2;
+        const int half = ew >> 2;  // which COLS-wide column slice of the tile
         EpiCtx cx;
         cx.lane = lane;
-        cx.stage = sStage + ew * 4096;
+        cx.stage = sStage + ew * C::STAGE_PER_WARP;
         cx.tmC = &tmC;
         uint32_t tb = 0, tph = 0;
         bool ok = true;
@@ -201,8 +203,9 @@ __global__ void __launch_bounds__(320, 1)
             const float *wsr = nullptr;
             if (PROMOTE) wsr = g.ws + (size_t)min(WS_ON_M ? mb : (cx.col0 >> 7), g.ws_rows - 1) * g.ws_ld;
             float snext = PROMOTE ? __ldg(wsr) : 1.0f;
+            const float amul = g.ascale * Epi::col_scale(ep, cx);  // activation dequant x the epilogue's own factor
             for (int u = 0; u < units; u++) {
-                const float s = PROMOTE ? g.ascale * snext : 1.0f;
+                const float s = PROMOTE ? amul * snext : 1.0f;
                 if (PROMOTE && u + 1 < units) snext = __ldg(wsr + u + 1);
                 // warp-uniform outcome: the tcgen05.ld below is a .sync.aligned warp instruction
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
@@ -256,6 +259,7 @@ struct EpiF32 {
         int ld, M, N;
     };
     using State = NoState;
+    __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {

@@ -266,6 +266,28 @@ __device__ __forceinline__ float tanh_fast(float x)
     return y;
 }
 
+// Packed fp32 pair arithmetic (sm_100: one instruction for two lanes' worth of fp32 work).
+__device__ __forceinline__ uint64_t f2_bits(float2 a) { return *reinterpret_cast<uint64_t *>(&a); }
+__device__ __forceinline__ float2 bits_f2(uint64_t b) { return *reinterpret_cast<float2 *>(&b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+    return bits_f2(d);
+}
+
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll
