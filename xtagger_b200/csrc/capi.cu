@@ -23,7 +23,7 @@ int xtb_gemm_e4m3_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, c
         fprintf(stderr, "eva: xtb_gemm_e4m3_f32: bad shape m %d n %d k %d (k must be a multiple of 16)\n", m, n, k);
         return -1;
     }
-    if (make_operand(&A, a, m, k, 128) || make_operand(&W.op, w, n, k, 256)) return -1;
+    if (make_operand(&A, a, m, k, A_BOX_ROWS) || make_operand(&W.op, w, n, k, weight_box_rows(W_F32))) return -1;
     W.ws = wscale;
     W.n = n;
     W.k = k;
@@ -39,12 +39,12 @@ static int rows_ok(int rows, const char *what)
     return 1;
 }
 
-static int weight(Weight8 *w, const uint8_t *p, int n, int k, const float *ws)
+static int weight(Weight8 *w, const uint8_t *p, int n, int k, const float *ws, WeightUse use)
 {
     w->ws = ws;
     w->n = n;
     w->k = k;
-    return make_operand(&w->op, p, n, k, 256);
+    return make_operand(&w->op, p, n, k, weight_box_rows(use));
 }
 
 int xtb_ln_e4m3(const uint16_t *x, const float *g, const float *b, uint8_t *y, int rows, float qs, void *stream)
@@ -58,7 +58,7 @@ int xtb_qkv(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float
 {
     Operand A;
     Weight8 W;
-    if (!rows_ok(rows, "xtb_qkv") || make_operand(&A, h, rows, D, 128) || weight(&W, w, 3 * D, D, ws)) return -1;
+    if (!rows_ok(rows, "xtb_qkv") || make_operand(&A, h, rows, D, 128) || weight(&W, w, 3 * D, D, ws, W_QKV)) return -1;
     return launch_qkv(A, W, ascale, rows, q8, k8, v8, cs, cq, ck, cv, S(stream));
 }
 
@@ -74,7 +74,7 @@ int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, flo
 {
     Operand A;
     Weight8 W;
-    if (!rows_ok(rows, "xtb_oproj") || make_operand(&A, a, rows, D, 128) || weight(&W, w, D, D, ws)) return -1;
+    if (!rows_ok(rows, "xtb_oproj") || make_operand(&A, a, rows, D, 128) || weight(&W, w, D, D, ws, W_O)) return -1;
     return launch_oproj(A, W, ascale, rows, (__half *)x, S(stream));
 }
 
@@ -83,7 +83,7 @@ int xtb_fc1(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float
 {
     Operand A;
     Weight8 W;
-    if (!rows_ok(rows, "xtb_fc1") || make_operand(&A, h, rows, D, 128) || weight(&W, w, N12, D, ws)) return -1;
+    if (!rows_ok(rows, "xtb_fc1") || make_operand(&A, h, rows, D, 128) || weight(&W, w, N12, D, ws, W_FC1)) return -1;
     return launch_fc1(A, W, ascale, rows, h8, (float2 *)stat, rs, S(stream));
 }
 
@@ -92,7 +92,7 @@ int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, floa
 {
     Operand A;
     Weight8 W;
-    if (!rows_ok(rows, "xtb_fc2") || make_operand(&A, h8, rows, HIDP, 128) || weight(&W, w, D, HIDP, ws)) return -1;
+    if (!rows_ok(rows, "xtb_fc2") || make_operand(&A, h8, rows, HIDP, 128) || weight(&W, w, D, HIDP, ws, W_FC2)) return -1;
     return launch_fc2(A, W, ascale, rows, (__half *)x, (float2 *)stat, c, d, S(stream));
 }
 

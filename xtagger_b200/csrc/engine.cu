@@ -203,7 +203,7 @@ int layout(Impl *im, Replica &r, const uint8_t *hostblob)
             L.w[g].ws = sp[g];
             L.w[g].n = n;
             L.w[g].k = k;
-            RCK(make_operand(&L.w[g].op, wp[g], n, k, 256));
+            RCK(make_operand(&L.w[g].op, wp[g], n, k, weight_box_rows((WeightUse)g)));  // g: W_QKV, W_O, W_FC1, W_FC2
             L.adq[g] = tb[4 + g];
         }
         L.cq = 1.0f / tb[8];

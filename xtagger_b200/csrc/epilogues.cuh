@@ -1,5 +1,6 @@
-// Fused GEMM epilogues of the EVA02-L forward (calling convention in gemm.cuh). Each one replaces a reference
-// kernel's epilogue, written for the tcgen05 GEMM's one-row-per-thread accumulator layout:
+// Fused GEMM epilogues of the EVA02-L forward (calling convention in gemm.cuh; the CTA-pair GEMM of gemm2.cuh
+// calls them the same way). Each one replaces a reference kernel's epilogue, written for the tcgen05 GEMM's
+// one-row-per-thread accumulator layout:
 //   EpiQKV    <- k_qkv   (eva_kernels.cu:41-114):  RoPE on q / k of patch tokens, E4M3, attention layouts
 //   EpiResid  <- k_oproj (eva_kernels.cu:134-162): fp16 residual += acc, as a TMA reduce-add into x
 //   EpiFC1    <- k_fc1   (eva_kernels.cu:211-279): SwiGLU, per-row LN statistics partials, E4M3 h (TMA store)
@@ -11,7 +12,7 @@
 // no epilogue thread waits on a load of x. Against the reference's x = fp16(x + delta) this rounds delta to fp16
 // first: at most half an fp16 ulp of delta, far below an ulp of x.
 #pragma once
-#include "gemm.cuh"
+#include "gemm2.cuh"
 #include "ops.h"
 
 namespace xtb {
@@ -34,47 +35,83 @@ struct EpiQKV {
         const int which = cx.col0 >> 10;
         return which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
     }
-    // pull the row's RoPE angles (256 bytes) into L1 while the accumulator is being built
+    // The RoPE angles of the warp's 32 rows (256 bytes each) are brought in through the staging buffer with
+    // coalesced loads, half a row (16 pairs) at a time: rows t of one warp are consecutive in the table, so each
+    // load instruction covers 4 whole 128-byte lines instead of 32 lines touched by one lane each.
+    __device__ __forceinline__ static void stage_angles(const Params &p, const EpiCtx &cx, int h)
+    {
+        const int t0 = cx.row0 % T;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = 4 * i + (cx.lane >> 3), c = cx.lane & 7;
+            int tt = t0 + r;
+            if (tt >= T) tt -= T;
+            float4 v = make_float4(1.f, 0.f, 1.f, 0.f);  // cls rows and rows past M: identity
+            if (tt > 0 && cx.row0 + r < p.M) v = __ldg((const float4 *)(p.cs + (size_t)(tt - 1) * 32 + 16 * h) + c);
+            *(float4 *)stage_chunk(cx.stage, r, c) = v;
+        }
+    }
+    // The first half is staged before the accumulator is built (the staging buffer is free between tiles: the
+    // previous tile's stores read it synchronously), so those loads overlap the main loop.
     __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &)
     {
-        const int row = cx.row0 + cx.lane, t = row % T;
-        if ((cx.col0 >> 10) < 2 && t > 0 && row < p.M) {
-            const char *a = (const char *)(p.cs + (size_t)(t - 1) * 32);
-            asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
-            asm volatile("prefetch.global.L1 [%0];" ::"l"(a + 128));
-        }
+        if ((cx.col0 >> 10) < 2) stage_angles(p, cx, 0);
     }
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
         const int which = cx.col0 >> 10;           // 0 q, 1 k, 2 v (a thread's 128 columns never straddle)
         const int head0 = (cx.col0 & 1023) >> 6;   // two heads per thread
-        const int row = cx.row0 + cx.lane;
-        const int t = row % T;
-        const bool rope = which < 2 && t > 0 && row < p.M;
-        const float4 *cs4 = (const float4 *)(p.cs + (size_t)(rope ? t - 1 : 0) * 32);
+        uint4 o[2][4];                             // E4M3 output: head hh, dims 16 q .. 16 q + 15
+        if (which == 2) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {          // 8 rotary pairs (16 dims) of both heads per step
-            float4 a[4];
+            for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) a[e] = rope ? __ldg(cs4 + (j >> 1) + e) : make_float4(1.f, 0.f, 1.f, 0.f);
+                for (int q = 0; q < 4; q++) {
+                    const float *a = acc + hh * 64 + 16 * q;
+                    uint32_t w[4];
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    float2 f[2];
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin) as two packed ops
-                        const float cosv = u ? a[e >> 1].z : a[e >> 1].x, sinv = u ? a[e >> 1].w : a[e >> 1].y;
-                        const float f0 = acc[hh * 64 + 2 * (j + e + u)], f1 = acc[hh * 64 + 2 * (j + e + u) + 1];
-                        f[u] = fma2(make_float2(f1, f0), make_float2(-sinv, sinv), mul2(make_float2(f0, f1), make_float2(cosv, cosv)));
-                    }
-                    w[e >> 1] = e4m3x2(f[0].x, f[0].y) | (e4m3x2(f[1].x, f[1].y) << 16);
+                    for (int e = 0; e < 4; e++) w[e] = e4m3x2(a[4 * e], a[4 * e + 1]) | (e4m3x2(a[4 * e + 2], a[4 * e + 3]) << 16);
+                    o[hh][q] = make_uint4(w[0], w[1], w[2], w[3]);
                 }
-                *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + (j >> 3)) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {          // pairs 16 h .. 16 h + 15 (half 0 was staged by begin)
+                __syncwarp();
+                if (h == 1) {
+                    stage_angles(p, cx, 1);
+                    __syncwarp();
+                }
+#pragma unroll
+                for (int q2 = 0; q2 < 2; q2++) {   // 8 pairs (16 dims of each head) per step
+                    float4 a[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) a[e] = *(const float4 *)stage_chunk(cx.stage, cx.lane, 4 * q2 + e);
+                    const int j = 16 * h + 8 * q2;
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 8; e += 2) {
+                            float2 f[2];
+#pragma unroll
+                            for (int u = 0; u < 2; u++) {
+                                // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin) as two packed ops
+                                const float cosv = u ? a[e >> 1].z : a[e >> 1].x, sinv = u ? a[e >> 1].w : a[e >> 1].y;
+                                const float f0 = acc[hh * 64 + 2 * (j + e + u)], f1 = acc[hh * 64 + 2 * (j + e + u) + 1];
+                                f[u] = fma2(make_float2(f1, f0), make_float2(-sinv, sinv), mul2(make_float2(f0, f1), make_float2(cosv, cosv)));
+                            }
+                            w[e >> 1] = e4m3x2(f[0].x, f[0].y) | (e4m3x2(f[1].x, f[1].y) << 16);
+                        }
+                        o[hh][2 * h + q2] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
             }
         }
+        __syncwarp();
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + q) = o[hh][q];
         __syncwarp();
         uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
 #pragma unroll

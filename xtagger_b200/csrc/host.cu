@@ -1,4 +1,5 @@
 #include <cudaTypedefs.h>
+#include <map>
 #include <mutex>
 #include "host.h"
 
@@ -58,6 +59,28 @@ int num_sms(int device)
         cache[device] = n;
     }
     return cache[device];
+}
+
+int max_pairs(const void *kern, int threads, size_t smem)
+{
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find({kern, dev});
+    if (it != cache.end()) return it->second;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms(dev), 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        fprintf(stderr, "eva: cudaOccupancyMaxActiveClusters failed on device %d\n", dev);
+        return 0;
+    }
+    cache[{kern, dev}] = n;
+    return n;
 }
 
 uint32_t *error_word(int device)

@@ -27,6 +27,10 @@ int make_tmap_2d_typed(CUtensorMap *m, const void *base, CUtensorMapDataType dt,
 
 int num_sms(int device);
 
+// Clusters of two CTAs of `kern` (threads, dynamic shared memory) that can be resident at once on the current
+// device (cudaOccupancyMaxActiveClusters), cached per (kernel, device); 0 on failure.
+int max_pairs(const void *kern, int threads, size_t smem);
+
 // Library error word on the given device (set by kernels whose bounded waits ran out).
 uint32_t *error_word(int device);
 

@@ -15,13 +15,12 @@
 // racing on one device) race on the array and must be serialised by the caller.
 //
 // Set-up: the first call on a device, with that device current, looks up the array's device address
-// (cudaGetSymbolAddress) and sets the GEMM kernel's shared-memory attribute; that first call should come before
-// any stream capture.
+// (cudaGetSymbolAddress), and the GEMM launcher sets its kernel's shared-memory attribute and reads how many CTAs
+// fit; that first call should come before any stream capture.
 #include <mutex>
 
 #include "../../include/xtagger_b200.h"
 #include "epilogues.cuh"
-#include "gemm.cuh"
 #include "host.h"
 #include "ops.h"
 
@@ -54,8 +53,6 @@ __global__ void __launch_bounds__(256) k_rowstat_into(const float2 *__restrict__
     ms[row] = make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
 }
 
-using Fc2Kernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, EpiFC2::Params);
-
 struct DeviceScratch {
     bool ready = false;
     NoAllocScratch *ptr = nullptr;
@@ -63,7 +60,8 @@ struct DeviceScratch {
 std::mutex g_mu;
 DeviceScratch g_dev[64];
 
-// Once per device, with the device current: the array's device address and the GEMM's shared-memory opt-in.
+// Once per device, with the device current: the array's device address. (The GEMM launcher sets its kernel's
+// shared-memory attribute itself on first use, without allocating.)
 int setup(int dev, NoAllocScratch **out)
 {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -77,12 +75,6 @@ int setup(int dev, NoAllocScratch **out)
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc);
         if (e != cudaSuccess || !p) {
             fprintf(stderr, "eva: xtb_fc2_noalloc: cudaGetSymbolAddress: %s\n", cudaGetErrorString(e));
-            return -1;
-        }
-        const Fc2Kernel k = k_gemm<EpiFC2, 256, false, true, false>;
-        e = cudaFuncSetAttribute((const void *)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GemmCfg<256>::SMEM);
-        if (e != cudaSuccess) {
-            fprintf(stderr, "eva: xtb_fc2_noalloc: cudaFuncSetAttribute: %s\n", cudaGetErrorString(e));
             return -1;
         }
         d.ptr = (NoAllocScratch *)p;
@@ -107,30 +99,18 @@ extern "C" int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, co
     NoAllocScratch *sc = nullptr;
     if (setup(dev, &sc)) return -1;
     cudaStream_t st = (cudaStream_t)stream;
-    Operand A, B;
+    Operand A;
+    Weight8 W;
     CUtensorMap xm;
-    if (make_operand(&A, h8, rows, HIDP, 128) || make_operand(&B, w, D, HIDP, 256) ||
-        make_tmap_2d_typed(&xm, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, (uint64_t)rows, D * 2, 64, 32,
-                           CU_TENSOR_MAP_SWIZZLE_128B))
+    W.ws = ws;
+    W.n = D;
+    W.k = HIDP;
+    if (make_operand(&A, h8, rows, HIDP, A_BOX_ROWS) || make_operand(&W.op, w, D, HIDP, weight_box_rows(W_FC2)) ||
+        resid_map(&xm, (__half *)x, rows))
         return -1;
     XTB_CK(cudaMemsetAsync(sc->status, 0, sizeof(sc->status), st));
     k_rowstat_into<<<(rows + 255) / 256, 256, 0, st>>>((const float2 *)stat, sc->ms, rows);
     XTB_CK(cudaGetLastError());
-    GemmArgs g;
-    g.M = rows;
-    g.N = D;
-    g.kiters = (HIDP + 127) / 128;
-    g.m_tiles = (rows + 127) / 128;
-    g.n_tiles = D / 256;
-    g.ws = ws;
-    g.ws_ld = (HIDP + 127) / 128;
-    g.ws_rows = D / 128;
-    g.ascale = ascale;
-    g.err = sc->status;
-    const int total = g.m_tiles * g.n_tiles;
-    const int grid = total < num_sms(dev) ? total : num_sms(dev);
-    EpiFC2::Params p{sc->ms, c, d, rows};
-    k_gemm<EpiFC2, 256, false, true, false><<<grid, GemmCfg<256>::THREADS, GemmCfg<256>::SMEM, st>>>(A.map, B.map, xm, g, p);
-    XTB_CK(cudaGetLastError());
+    if (launch_fc2_gemm(A, W, ascale, rows, xm, sc->ms, c, d, sc->status, st)) return -1;
     return 0;
 }

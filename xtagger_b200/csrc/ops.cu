@@ -23,6 +23,7 @@ int make_operand(Operand *op, const void *ptr, int rows, int row_bytes, int box_
     op->ptr = ptr;
     op->rows = rows;
     op->row_bytes = row_bytes;
+    op->box_rows = box_rows;
     return make_tmap_2d(&op->map, ptr, (uint64_t)row_bytes, (uint64_t)rows, (uint64_t)row_bytes, 128, (uint32_t)box_rows,
                         CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -43,13 +44,15 @@ static int set_smem(const void *kern, size_t bytes)
 // One launch of the tcgen05 GEMM: A = a (M rows), B = b (N rows), K slices of 128 bytes.
 template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
 static int run_gemm(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
-                    const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr)
+                    const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
+                    uint32_t *err = nullptr)
 {
     using Cfg = GemmCfg<BN>;
     auto kern = k_gemm<Epi, BN, F16, PROMOTE, WS_ON_M>;
     if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
-    if (a.row_bytes != b.row_bytes || M <= 0 || N <= 0) {
-        fprintf(stderr, "eva: gemm shape mismatch (K bytes %d vs %d, M %d, N %d)\n", a.row_bytes, b.row_bytes, M, N);
+    if (a.row_bytes != b.row_bytes || M <= 0 || N <= 0 || a.box_rows != A_BOX_ROWS || b.box_rows != BN) {
+        fprintf(stderr, "eva: gemm operands (K bytes %d vs %d, boxes %d / %d rows, M %d, N %d)\n", a.row_bytes,
+                b.row_bytes, a.box_rows, b.box_rows, M, N);
         return -1;
     }
     const int dev = current_device();
@@ -63,7 +66,7 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     g.ws_ld = ws_ld;
     g.ws_rows = ws_rows;
     g.ascale = ascale;
-    g.err = error_word(dev);
+    g.err = err ? err : error_word(dev);
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
@@ -72,12 +75,76 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     return 0;
 }
 
+// One launch of the CTA-pair GEMM (block-scaled E4M3): 256 x 128 tiles, one cluster of two CTAs per tile at a
+// time, as many clusters as can be resident (a persistent grid).
+template <class Epi>
+static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
+                     const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
+                     uint32_t *err = nullptr)
+{
+    using Cfg = Gemm2Cfg;
+    auto kern = k_gemm2<Epi, true>;
+    if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
+    if (a.row_bytes != b.row_bytes || M <= 0 || N <= 0 || a.box_rows != A_BOX_ROWS || b.box_rows != Cfg::BN / 2) {
+        fprintf(stderr, "eva: pair gemm operands (K bytes %d vs %d, boxes %d / %d rows, M %d, N %d)\n", a.row_bytes,
+                b.row_bytes, a.box_rows, b.box_rows, M, N);
+        return -1;
+    }
+    const int dev = current_device();
+    GemmArgs g;
+    g.M = M;
+    g.N = N;
+    g.kiters = (a.row_bytes + 127) / 128;
+    g.m_tiles = (M + 255) / 256;
+    g.n_tiles = (N + Cfg::BN - 1) / Cfg::BN;
+    g.ws = ws;
+    g.ws_ld = ws_ld;
+    g.ws_rows = ws_rows;
+    g.ascale = ascale;
+    g.err = err ? err : error_word(dev);
+    const int total = g.m_tiles * g.n_tiles;
+    int pairs = max_pairs((const void *)kern, Cfg::THREADS, Cfg::SMEM);
+    if (pairs <= 0) return -1;
+    if (pairs > total) pairs = total;
+    kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, b.map, tmc ? *tmc : a.map, g, ep);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
 static int kb(int k) { return (k + 127) / 128; }
+
+// Kernel of each projection (true: CTA pair), from timing both inside the batch-64 forward: the pair wins where the
+// operand feed bounds the main loop (fc2: K = 2736, A streamed from DRAM, 5.6 against 6.4 ms per forward) and for
+// QKV (7.45 against 7.7 ms); the single CTA for fc1 (10.3 against 10.8 ms) and O (2.14 against 2.19 ms).
+#ifndef XTB_PAIR_MASK
+#define XTB_PAIR_MASK 0x9  // bit u set: WeightUse u on the CTA-pair GEMM (QKV, fc2)
+#endif
+static constexpr bool kPair[5] = {(XTB_PAIR_MASK & 1) != 0, (XTB_PAIR_MASK & 2) != 0, (XTB_PAIR_MASK & 4) != 0,
+                                  (XTB_PAIR_MASK & 8) != 0, (XTB_PAIR_MASK & 16) != 0};
+
+int weight_box_rows(WeightUse u) { return kPair[u] ? Gemm2Cfg::BN / 2 : 256; }
+
+template <class Epi, WeightUse U>
+static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep, cudaStream_t st,
+                    const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
+{
+    if constexpr (kPair[U])
+        return run_gemm2<Epi>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
+    else
+        return run_gemm<Epi, 256, false, true, false>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
+}
+
+template <class Epi, WeightUse U>
+static const void *proj_kernel()
+{
+    if constexpr (kPair[U]) return (const void *)k_gemm2<Epi, true>;
+    else return (const void *)k_gemm<Epi, 256, false, true, false>;
+}
 
 int launch_gemm_f32(const Operand &a, const Weight8 &w, float ascale, float *out, int ldo, cudaStream_t st)
 {
     EpiF32<128>::Params p{out, ldo, a.rows, w.n};
-    return run_gemm<EpiF32<128>, 256, false, true, false>(a, w.op, a.rows, w.n, w.ws, kb(w.k), kb(w.n), ascale, p, st);
+    return run_proj<EpiF32<128>, W_F32>(a, w, a.rows, ascale, p, st);
 }
 
 int launch_patch_embed(const Operand &in, const Operand &pe, int nimg, const float *pos, __half *x, cudaStream_t st)
@@ -97,7 +164,7 @@ int launch_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, uint8
                const float *cs, float cq, float ck, float cv, cudaStream_t st)
 {
     EpiQKV::Params p{q8, k8, v8, (const float2 *)cs, cq, ck, cv, rows};
-    return run_gemm<EpiQKV, 256, false, true, false>(h, w.op, rows, 3 * D, w.ws, kb(w.k), kb(w.n), ascale, p, st);
+    return run_proj<EpiQKV, W_QKV>(h, w, rows, ascale, p, st);
 }
 
 int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg)
@@ -119,7 +186,7 @@ int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo
 }
 
 // The fp16 residual x [rows][1024] as the target of TMA reduce-adds: boxes of 64 halves x 32 rows, 128B swizzle.
-static int resid_map(CUtensorMap *m, __half *x, int rows)
+int resid_map(CUtensorMap *m, __half *x, int rows)
 {
     return make_tmap_2d_typed(m, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, (uint64_t)rows, D * 2, 64, 32,
                               CU_TENSOR_MAP_SWIZZLE_128B);
@@ -130,7 +197,7 @@ int launch_oproj(const Operand &a, const Weight8 &w, float ascale, int rows, __h
     CUtensorMap xm;
     if (resid_map(&xm, x, rows)) return -1;
     EpiResid::Params p{rows};
-    return run_gemm<EpiResid, 256, false, true, false>(a, w.op, rows, D, w.ws, kb(w.k), kb(w.n), ascale, p, st, &xm);
+    return run_proj<EpiResid, W_O>(a, w, rows, ascale, p, st, &xm);
 }
 
 int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
@@ -139,7 +206,7 @@ int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8
     CUtensorMap hm;  // h8 [rows][2736] E4M3, stored in boxes of 64 units x 32 rows (64B swizzle)
     if (make_tmap_2d(&hm, h8, HIDP, (uint64_t)rows, HIDP, 64, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     EpiFC1::Params p{stat, rs, rows};
-    return run_gemm<EpiFC1, 256, false, true, false>(h, w.op, rows, N12, w.ws, kb(w.k), kb(w.n), ascale, p, st, &hm);
+    return run_proj<EpiFC1, W_FC1>(h, w, rows, ascale, p, st, &hm);
 }
 
 int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
@@ -149,8 +216,14 @@ int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __ha
     if (resid_map(&xm, x, rows)) return -1;
     k_rowstat<<<(rows + 255) / 256, 256, 0, st>>>(stat, rows);
     XTB_CK(cudaGetLastError());
-    EpiFC2::Params p{stat, c, d, rows};
-    return run_gemm<EpiFC2, 256, false, true, false>(h8, w.op, rows, D, w.ws, kb(w.k), kb(w.n), ascale, p, st, &xm);
+    return launch_fc2_gemm(h8, w, ascale, rows, xm, stat, c, d, nullptr, st);
+}
+
+int launch_fc2_gemm(const Operand &h8, const Weight8 &w, float ascale, int rows, const CUtensorMap &xm, const float2 *ms,
+                    const float *c, const float *d, uint32_t *err, cudaStream_t st)
+{
+    EpiFC2::Params p{ms, c, d, rows};
+    return run_proj<EpiFC2, W_FC2>(h8, w, rows, ascale, p, st, &xm, err);
 }
 
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
@@ -185,12 +258,22 @@ int prepare_kernels()
         fprintf(stderr, "eva: cannot set up the error word on device %d\n", dev);
         return -1;
     }
-    const void *g256[] = {
-        (const void *)k_gemm<EpiF32<128>, 256, false, true, false>, (const void *)k_gemm<EpiPatch, 256, true, false, false>,
-        (const void *)k_gemm<EpiQKV, 256, false, true, false>,      (const void *)k_gemm<EpiResid, 256, false, true, false>,
-        (const void *)k_gemm<EpiFC1, 256, false, true, false>,      (const void *)k_gemm<EpiFC2, 256, false, true, false>};
-    for (const void *k : g256)
+    const void *single[] = {(const void *)k_gemm<EpiPatch, 256, true, false, false>};
+    for (const void *k : single)
         if (set_smem(k, GemmCfg<256>::SMEM)) return -1;
+    const void *proj[5];  // indexed by WeightUse
+    proj[W_QKV] = proj_kernel<EpiQKV, W_QKV>();
+    proj[W_O] = proj_kernel<EpiResid, W_O>();
+    proj[W_FC1] = proj_kernel<EpiFC1, W_FC1>();
+    proj[W_FC2] = proj_kernel<EpiFC2, W_FC2>();
+    proj[W_F32] = proj_kernel<EpiF32<128>, W_F32>();
+    for (int u = 0; u < 5; u++) {
+        if (!kPair[u]) {
+            if (set_smem(proj[u], GemmCfg<256>::SMEM)) return -1;
+        } else if (set_smem(proj[u], Gemm2Cfg::SMEM) || max_pairs(proj[u], Gemm2Cfg::THREADS, Gemm2Cfg::SMEM) <= 0) {
+            return -1;
+        }
+    }
     const void *g64[] = {(const void *)k_gemm<EpiHead<32>, 64, true, false, false>,
                          (const void *)k_gemm<EpiHead<32>, 64, false, true, true>};
     for (const void *k : g64)

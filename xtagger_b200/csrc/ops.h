@@ -19,9 +19,17 @@ constexpr int QT = (T + 127) / 128;               // 128-query tiles per (image,
 struct Operand {
     CUtensorMap map;
     const void *ptr;
-    int rows, row_bytes;
+    int rows, row_bytes, box_rows;
 };
+// Box height of every A (activation) operand.
+constexpr int A_BOX_ROWS = 128;
 int make_operand(Operand *op, const void *ptr, int rows, int row_bytes, int box_rows);
+
+// The block-scaled projections. Each runs on the GEMM kernel measured fastest for its shape (the single-CTA
+// 128 x 256 tile of gemm.cuh, or the 256 x 256 CTA-pair tile of gemm2.cuh), which fixes the box height its weight
+// operand is read in: weight_box_rows(use).
+enum WeightUse { W_QKV = 0, W_O = 1, W_FC1 = 2, W_FC2 = 3, W_F32 = 4 };
+int weight_box_rows(WeightUse u);
 
 // Block-scaled weight: E4M3 [n][k] plus fp32 scales [ceil(n / 128)][ceil(k / 128)].
 struct Weight8 {
@@ -48,6 +56,12 @@ int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8
 // stat: fc1's [NSTAT][rows] partials; consumed (row (mean, rstd) written into partial 0) before the GEMM.
 int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
                const float *d, cudaStream_t st);
+// The fc2 GEMM alone, with (mean, rstd) per row already in ms and bounded-wait failures reported in *err: for
+// callers that keep that scratch themselves (xtb_fc2_noalloc). Allocates nothing.
+int launch_fc2_gemm(const Operand &h8, const Weight8 &w, float ascale, int rows, const CUtensorMap &xm, const float2 *ms,
+                    const float *c, const float *d, uint32_t *err, cudaStream_t st);
+// The fp16 residual x [rows][1024] as the target of TMA reduce-adds.
+int resid_map(CUtensorMap *m, __half *x, int rows);
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
                    float qs_head, cudaStream_t st);
 int launch_head_f16(const Operand &hw, const Operand &pn, int nimg, int nt, const float *hb, float *out,

@@ -211,6 +211,81 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------------------------
+// CTA pairs (clusters of two CTAs on the two SMs of a TPC, tcgen05 .cta_group::2). A kernel uses either these
+// forms or the .cta_group::1 forms above for all of its tcgen05 instructions, never both.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of both CTAs (converged warps): release this CTA's prior writes / acquire the peer's.
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address, in the cluster's shared window, of the object at the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+// Arrive on an mbarrier of either CTA of the cluster (cluster-window address). The default (CTA-scope) forms are
+// enough for every hand-off of the pair GEMM: shared-memory tiles are published by the TMA's complete_tx, TMEM
+// reads and writes are ordered by the tcgen05 fences around the barrier; cluster-scope acquire / release on these
+// barriers made the pair GEMM three times slower.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t caddr, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(caddr), "r"(bytes) : "memory");
+}
+// 2D tile load into this CTA's shared memory whose completion is counted on an mbarrier of either CTA of the pair
+// (cluster-window address). No multicast: each CTA loads only its own tiles.
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m, uint32_t bar_caddr, int32_t x, int32_t y)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.cta_group::2 [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"((uint64_t)m), "r"(bar_caddr), "r"(x), "r"(y)
+        : "memory");
+}
+// One warp in each CTA of the pair, together: allocate / free ncols TMEM columns in both CTAs.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Pair MMA (issued by rank 0 for both CTAs), E4M3 x E4M3 -> f32: A rows from each CTA's own shared memory, B rows
+// from both, D rows of each CTA in its own TMEM; descriptors give the (identical) shared-memory offsets.
+__device__ __forceinline__ void umma_pair_e4m3(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier at this shared-memory offset in every CTA of `mask` when the pair MMAs issued so far
+// have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar, uint16_t mask)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem_u32(bar)),
+                 "h"(mask)
+                 : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with a 128-byte (sw = 2) or 64-byte
@@ -248,6 +323,11 @@ __device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t sbo_bytes,
 __host__ __device__ constexpr uint32_t idesc_m128(uint32_t n)
 {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+// The same for a CTA-pair MMA of M = 256 (128 rows per CTA).
+__host__ __device__ constexpr uint32_t idesc_m256(uint32_t n)
+{
+    return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((256u >> 4) << 24);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
