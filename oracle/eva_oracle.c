@@ -221,64 +221,87 @@ void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, floa
 }
 
 /* ---------------------------------------------------------------------------------------------------------------
- * Attention (flash8, kern_common.cuh:403-543), per query row, keys in tiles of key_tile:
- *   m = -1e30, l = 0, O = 0; per tile: tm = max of the row's scores (keys < 1025)
- *   if tm > m + RESCALE / sinv:  sc = exp2((m - tm) sinv); l *= sc; O *= sc; m = tm           (lazy rescale)
- *   if tm < m - PSKIP / sinv: the tile adds nothing (every p rounds to zero in E4M3)           (dead tile)
- *   else p = exp2((s - m) sinv); l += p; O += E4M3(p) * V
- *   out = fp16(O * vo / l) -> E4M3 (the reference stages the output as fp16, kern_common.cuh:527-541).
- * The reference takes the rescale decision per 16-row warp slice; this library's kernel per row, as here.
+ * Attention (flash8, kern_common.cuh:403-543). Query rows go in slices of slice_rows consecutive rows (the reference:
+ * 16, one warp's rows, kern_common.cuh:433-434 and 470-481; slices start at multiples of slice_rows and run past
+ * token 1024 into the zero query rows of the padding, which take part in the decisions as in the reference), keys
+ * in tiles of key_tile (the reference: 64):
+ *   m = -1e30, l = 0, O = 0 per row; per tile: tm = max of the row's scores over the tile's keys (< 1025)
+ *   lazy rescale (kern_common.cuh:484-493): if some row of the slice has max(m, tm) > m + RESCALE / sinv, every
+ *     row of the slice takes mn = max(m, tm): sc = exp2((m - mn) sinv); l *= sc; O *= sc; m = mn
+ *   dead tile (kern_common.cuh:496-499): if every row of the slice has tm < m - PSKIP / sinv, the tile adds nothing
+ *   else, every row: p = exp2(s sinv - m sinv) (one fma); l += p; O += E4M3(p) * V
+ *   out = E4M3(fp16(O * (vo / l))) (the reference stages the output as fp16, kern_common.cuh:527-541).
  * ------------------------------------------------------------------------------------------------------------- */
 void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg, float sinv, float vo,
-                  int key_tile, uint8_t *out)
+                  int key_tile, int slice_rows, uint8_t *out)
 {
     float lut[256];
     for (int i = 0; i < 256; i++) lut[i] = or_e4m3_dec((uint8_t)i);
     const float thr = RESCALE / sinv, dthr = PSKIP / sinv;
+    const int SR = slice_rows, nslices = (OR_T + SR - 1) / SR;
 #pragma omp parallel for collapse(2) schedule(dynamic)
     for (int b = 0; b < nimg; b++)
         for (int h = 0; h < OR_NH; h++) {
             const size_t bh = (size_t)b * OR_NH + h;
-            float *K = malloc((size_t)OR_T * 64 * 4), *V = malloc((size_t)OR_T * 64 * 4), *S = malloc(OR_T * 4);
+            float *K = malloc((size_t)OR_T * 64 * 4), *V = malloc((size_t)OR_T * 64 * 4);
+            float *S = malloc((size_t)SR * OR_T * 4), *o = malloc((size_t)SR * 64 * 4);
+            float *m = malloc(SR * 4), *l = malloc(SR * 4), *tm = malloc(SR * 4);
             for (int t = 0; t < OR_T; t++)
                 for (int d = 0; d < 64; d++) {
                     K[t * 64 + d] = lut[k8[(bh * OR_TP + t) * 64 + d]];
                     V[t * 64 + d] = lut[v8[(bh * OR_TP + t) * 64 + d]];
                 }
-            for (int qi = 0; qi < OR_T; qi++) {
-                float q[64], o[64];
-                for (int d = 0; d < 64; d++) {
-                    q[d] = lut[q8[(bh * OR_TP + qi) * 64 + d]];
-                    o[d] = 0.f;
+            for (int g = 0; g < nslices; g++) {
+                for (int i = 0; i < SR; i++) {   /* rows past 1024 read the zero padding of q8 (1152 rows) */
+                    float q[64];
+                    for (int d = 0; d < 64; d++) q[d] = lut[q8[(bh * OR_TP + g * SR + i) * 64 + d]];
+                    for (int t = 0; t < OR_T; t++) S[i * OR_T + t] = dotf(q, K + t * 64, 64);
+                    for (int d = 0; d < 64; d++) o[i * 64 + d] = 0.f;
+                    m[i] = -1e30f;
+                    l[i] = 0.f;
                 }
-                for (int t = 0; t < OR_T; t++) S[t] = dotf(q, K + t * 64, 64);
-                float m = -1e30f, l = 0.f;
                 for (int t0 = 0; t0 < OR_T; t0 += key_tile) {
                     const int t1 = t0 + key_tile < OR_T ? t0 + key_tile : OR_T;
-                    float tm = -INFINITY;
-                    for (int t = t0; t < t1; t++) tm = fmaxf(tm, S[t]);
-                    if (tm > m + thr) {
-                        const float sc = exp2f((m - tm) * sinv);
-                        l *= sc;
-                        for (int d = 0; d < 64; d++) o[d] *= sc;
-                        m = tm;
+                    int resc = 0, dead = 1;
+                    for (int i = 0; i < SR; i++) {
+                        tm[i] = -INFINITY;
+                        for (int t = t0; t < t1; t++) tm[i] = fmaxf(tm[i], S[i * OR_T + t]);
+                        if (fmaxf(m[i], tm[i]) > m[i] + thr) resc = 1;
                     }
-                    if (tm < m - dthr) continue;
-                    for (int t = t0; t < t1; t++) {
-                        const float p = exp2f(fmaf(S[t], sinv, -m * sinv));
-                        l += p;
-                        const float pq = lut[or_e4m3(p)];
-                        if (pq != 0.f)
-                            for (int d = 0; d < 64; d++) o[d] += pq * V[t * 64 + d];
-                    }
+                    if (resc)
+                        for (int i = 0; i < SR; i++) {
+                            const float mn = fmaxf(m[i], tm[i]), sc = exp2f((m[i] - mn) * sinv);
+                            l[i] *= sc;
+                            for (int d = 0; d < 64; d++) o[i * 64 + d] *= sc;
+                            m[i] = mn;
+                        }
+                    for (int i = 0; i < SR; i++)
+                        if (!(tm[i] < m[i] - dthr)) dead = 0;
+                    if (dead) continue;
+                    for (int i = 0; i < SR; i++)
+                        for (int t = t0; t < t1; t++) {
+                            const float p = exp2f(fmaf(S[i * OR_T + t], sinv, -m[i] * sinv));
+                            l[i] += p;
+                            const float pq = lut[or_e4m3(p)];
+                            if (pq != 0.f)
+                                for (int d = 0; d < 64; d++) o[i * 64 + d] += pq * V[t * 64 + d];
+                        }
                 }
-                const float f = vo / l;
-                uint8_t *dst = out + ((size_t)b * OR_T + qi) * OR_D + h * 64;
-                for (int d = 0; d < 64; d++) dst[d] = or_e4m3(h16r(o[d] * f));
+                for (int i = 0; i < SR; i++) {
+                    const int qi = g * SR + i;
+                    if (qi >= OR_T) break;
+                    const float f = vo / l[i];
+                    uint8_t *dst = out + ((size_t)b * OR_T + qi) * OR_D + h * 64;
+                    for (int d = 0; d < 64; d++) dst[d] = or_e4m3(h16r(o[i * 64 + d] * f));
+                }
             }
             free(K);
             free(V);
             free(S);
+            free(o);
+            free(m);
+            free(l);
+            free(tm);
         }
 }
 
@@ -546,7 +569,8 @@ int or_model_nt(const char *model)
 }
 
 /* The forward of eva_forward (eva.h:252-307) for nimg inputs. */
-int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, float *scores, uint16_t *pn_out)
+int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, int slice_rows, float *scores,
+               uint16_t *pn_out)
 {
     or_model M;
     if (model_load(model, &M)) return -1;
@@ -564,7 +588,7 @@ int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, fl
         or_ln_e4m3(x, L->ln1w, L->ln1b, rows, 1.0f / L->adq[0], h);
         or_gemm_e4m3(h, rows, OR_D, L->wqkv, 3 * OR_D, L->sqkv, L->adq[0], acc);
         or_qkv_epilogue(acc, rows, M.cs, L->cq, L->ck, L->cv, q8, k8, v8);
-        or_attention(q8, k8, v8, nimg, L->sinv, L->vo, key_tile, h);
+        or_attention(q8, k8, v8, nimg, L->sinv, L->vo, key_tile, slice_rows, h);
         or_gemm_e4m3(h, rows, OR_D, L->wo, OR_D, L->so, L->adq[1], acc);
         or_resid_add(x, acc, rows);
         or_ln_e4m3(x, L->ln2w, L->ln2b, rows, 1.0f / L->adq[2], h);

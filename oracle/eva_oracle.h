@@ -40,8 +40,9 @@ void or_gemm_f16(const uint16_t *a, int m, int k, const uint16_t *w, int n, floa
 void or_ln_e4m3(const uint16_t *x, const float *g, const float *b, int rows, float qs, uint8_t *y);
 void or_qkv_epilogue(const float *acc, int rows, const float *cs, float cq, float ck, float cv, uint8_t *q8,
                      uint8_t *k8, uint8_t *v8);
+/* key_tile keys per tile and decisions per slice of slice_rows query rows: 64 and 16 are the reference's */
 void or_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg, float sinv, float vo,
-                  int key_tile, uint8_t *out);
+                  int key_tile, int slice_rows, uint8_t *out);
 void or_resid_add(uint16_t *x, const float *acc, int rows);
 void or_fc1_epilogue(const float *acc, int rows, const float *rs, uint8_t *h8, double *rowsum, double *rowsq);
 void or_fc2_epilogue(uint16_t *x, const float *acc, int rows, const double *rowsum, const double *rowsq,
@@ -54,9 +55,10 @@ void or_head_e4m3(const uint8_t *pn8, int nimg, const uint8_t *hw8, const float 
                   int nt, float *out);
 
 /* whole forward from a model file (eva02.bin v3 or the block-scaled v4); in: nimg x [1024][592] fp16.
- * scores [nimg][nt]; pn (optional) [nimg][1024] fp16. key_tile: 128 (this library's attention tiling) or 64
- * (the reference's). Returns 0, or -1 with a message on stderr. */
-int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, float *scores, uint16_t *pn);
+ * scores [nimg][nt]; pn (optional) [nimg][1024] fp16. key_tile / slice_rows: the attention's key tiling and
+ * decision slices (64 / 16: the reference's). Returns 0, or -1 with a message on stderr. */
+int or_forward(const char *model, const uint16_t *in, int nimg, int key_tile, int slice_rows, float *scores,
+               uint16_t *pn);
 /* number of tags of a model file (-1 on error) */
 int or_model_nt(const char *model);
 

@@ -41,7 +41,7 @@ def lib():
             "or_gemm_f16": (None, [_u16, C.c_int, C.c_int, _u16, C.c_int, _f32]),
             "or_ln_e4m3": (None, [_u16, _f32, _f32, C.c_int, C.c_float, _u8]),
             "or_qkv_epilogue": (None, [_f32, C.c_int, _f32, C.c_float, C.c_float, C.c_float, _u8, _u8, _u8]),
-            "or_attention": (None, [_u8, _u8, _u8, C.c_int, C.c_float, C.c_float, C.c_int, _u8]),
+            "or_attention": (None, [_u8, _u8, _u8, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, _u8]),
             "or_resid_add": (None, [_u16, _f32, C.c_int]),
             "or_fc1_epilogue": (None, [_f32, C.c_int, _f32, _u8, _f64, _f64]),
             "or_fc2_epilogue": (None, [_u16, _f32, C.c_int, _f64, _f64, _f32, _f32]),
@@ -49,7 +49,7 @@ def lib():
             "or_pool_ln": (None, [_u16, C.c_int, _f32, _f32, _f32, _u16, C.c_void_p, C.c_float]),
             "or_head_f16": (None, [_u16, C.c_int, _u16, _f32, C.c_int, _f32]),
             "or_head_e4m3": (None, [_u8, C.c_int, _u8, _f32, C.c_float, _f32, C.c_int, _f32]),
-            "or_forward": (C.c_int, [C.c_char_p, _u16, C.c_int, C.c_int, _f32, C.c_void_p]),
+            "or_forward": (C.c_int, [C.c_char_p, _u16, C.c_int, C.c_int, C.c_int, _f32, C.c_void_p]),
             "or_model_nt": (C.c_int, [C.c_char_p]),
             "or_prune24": (None, [_u8, C.c_int, C.c_int, C.c_int]),
             "or_threads": (C.c_int, []),
@@ -93,8 +93,9 @@ def gemm_f16(a, w):
     return out
 
 
-def forward(model, inputs, key_tile=128, want_pn=False):
-    """Scores [nimg][nt] (and fp16 pn [nimg][1024]) of the whole forward on the CPU."""
+def forward(model, inputs, key_tile=64, slice_rows=16, want_pn=False):
+    """Scores [nimg][nt] (and fp16 pn [nimg][1024]) of the whole forward on the CPU. The defaults are the
+    reference's attention: 64-key tiles, lazy-rescale / dead-tile decisions per 16-row warp slice."""
     inputs = np.ascontiguousarray(inputs, np.uint16)
     nimg = inputs.shape[0]
     nt = lib().or_model_nt(model.encode())
@@ -102,7 +103,7 @@ def forward(model, inputs, key_tile=128, want_pn=False):
         raise RuntimeError(f"oracle cannot read {model}")
     scores = np.empty((nimg, nt), np.float32)
     pn = np.empty((nimg, 1024), np.uint16) if want_pn else None
-    rc = lib().or_forward(model.encode(), inputs.ravel(), nimg, key_tile, scores,
+    rc = lib().or_forward(model.encode(), inputs.ravel(), nimg, key_tile, slice_rows, scores,
                           pn.ctypes.data_as(C.c_void_p) if want_pn else None)
     if rc:
         raise RuntimeError("oracle forward failed")

@@ -42,8 +42,8 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     from xtagger_b200 import model as M
     from xtagger_b200.engine import Engine
     x = M.synthetic_inputs(nimg, seed=21)
-    want = O.forward(models[name], x, key_tile=128)
-    alt = O.forward(models[name], x, key_tile=64)        # the reference's tiling of the same semantics
+    want = O.forward(models[name], x)                     # the reference's attention: 64-key tiles, 16-row slices
+    alt = O.forward(models[name], x, key_tile=128, slice_rows=1)   # another tiling of the same arithmetic
     floor_max = float(np.abs(alt - want).max())
     floor_mean = float(np.abs(alt - want).mean())
     eng = Engine(models[name], nb=max(nimg, 2))
@@ -55,7 +55,7 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     assert np.isfinite(got).all()
     err = np.abs(got - want)
     print(f"{name}: engine-vs-oracle max {err.max():.2e} mean {err.mean():.2e}; "
-          f"oracle64-vs-oracle128 max {floor_max:.2e} mean {floor_mean:.2e}")
+          f"oracle tiling sensitivity max {floor_max:.2e} mean {floor_mean:.2e}")
     tol_max = max(2e-3, 1.5 * floor_max)
     assert err.max() <= tol_max
     assert err.mean() <= max(2e-4, 1.5 * floor_mean)
@@ -102,7 +102,7 @@ def test_teacher_forced_layers(xlib, cuda, models):
         assert xlib.xtb_attention(G.P(q8), G.P(k8), G.P(vt8), nimg, G.P(att), float(L["sinv"]), float(L["vo"]),
                                   None) == 0
         aw = np.empty((rows, 1024), np.uint8)
-        lib.or_attention(qg, kg, vg, nimg, float(L["sinv"]), float(L["vo"]), 128, aw)
+        lib.or_attention(qg, kg, vg, nimg, float(L["sinv"]), float(L["vo"]), 64, 16, aw)
         G.assert_attention_close(G.host(att), aw, f"L{i} attention")
         ag = G.host(att).copy()
         assert xlib.xtb_oproj(G.P(att), rows, G.P(G.dev(L["o"])), G.P(G.dev(L["o_s"])), float(L["adq"][1]), G.P(x),

@@ -86,7 +86,7 @@ def test_attention(xlib, cuda, O, peaked):
     sinv = (0.8 / 448) * (4.0 / 448)
     vo = (448 / 3.0) * (3.0 / 448) * 0.9
     want = np.empty((ROWS, D), np.uint8)
-    O.lib().or_attention(q, k, vt, NIMG, sinv, vo, 128, want)
+    O.lib().or_attention(q, k, vt, NIMG, sinv, vo, 64, 16, want)   # the reference's tiling and slices
     out = G.zeros((ROWS, D), torch.uint8)
     assert xlib.xtb_attention(G.P(G.dev(q)), G.P(G.dev(k)), G.P(G.dev(vt)), NIMG, G.P(out), sinv, vo, None) == 0
     G.check_error_word(xlib)

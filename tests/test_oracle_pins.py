@@ -92,9 +92,43 @@ def test_gemm_blockscaled_matches_numpy(O):
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6 * np.abs(want).max())
 
 
-def test_attention_matches_numpy_restatement(O):
-    """The oracle's flash attention (tiles, lazy rescale, dead tiles, E4M3 P) against a vectorised numpy statement
-    of the same algorithm, for one head."""
+def _attention_numpy(O, q, k, v, sinv, vo, key_tile, slice_rows, head):
+    """flash8's algorithm (kern_common.cuh:403-543) for one head, vectorised over slices of slice_rows query rows:
+    decisions (lazy rescale, dead tile) per slice and key tile, as the oracle's C restatement."""
+    TP, T = q.shape[2], 1025
+    ns = -(-T // slice_rows)
+    R = ns * slice_rows                                  # rows past 1024 are the zero padding of q
+    Q = O.e4m3_dec(q[0, head, :R]).astype(np.float32)
+    K, V = (O.e4m3_dec(a[0, head, :T]).astype(np.float32) for a in (k, v))
+    S = (Q @ K.T).reshape(ns, slice_rows, T)
+    m = np.full((ns, slice_rows), -1e30, np.float32)
+    l = np.zeros((ns, slice_rows), np.float32)
+    acc = np.zeros((ns, slice_rows, 64), np.float32)
+    thr, dthr = np.float32(8.0 / sinv), np.float32(10.0 / sinv)
+    with np.errstate(over="ignore", invalid="ignore"):
+        for t0 in range(0, T, key_tile):
+            s = S[:, :, t0:t0 + key_tile]
+            tm = s.max(2)
+            mn = np.maximum(m, tm)
+            re = (mn > m + thr).any(1)                   # per slice
+            sc = np.exp2((m - mn) * np.float32(sinv)).astype(np.float32)
+            l = np.where(re[:, None], l * sc, l)
+            acc = np.where(re[:, None, None], acc * sc[:, :, None], acc)
+            m = np.where(re[:, None], mn, m)
+            live = ~(tm < m - dthr).all(1)               # per slice
+            p = np.exp2(s * np.float32(sinv) - (m * np.float32(sinv))[:, :, None]).astype(np.float32)
+            p = np.where(live[:, None, None], p, 0)
+            l = l + p.sum(2)
+            acc = acc + O.e4m3_dec(O.e4m3(p)) @ V[t0:t0 + key_tile]
+    out = (acc * (vo / l)[:, :, None]).reshape(R, 64)[:T]
+    return O.e4m3(out.astype(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("key_tile,slice_rows", [(64, 16), (128, 1)])
+def test_attention_matches_numpy_restatement(O, key_tile, slice_rows):
+    """The oracle's flash attention (tiles, lazy rescale and dead tiles decided per slice of query rows, E4M3 P,
+    fp16-staged output) against a vectorised numpy statement of the same algorithm, for one head: the reference's
+    64-key tiles with 16-row slices, and 128-key tiles decided per row."""
     rng = np.random.default_rng(6)
     TP, T = 1152, 1025
     q = np.zeros((1, 16, TP, 64), np.uint8)
@@ -105,27 +139,8 @@ def test_attention_matches_numpy_restatement(O):
     v[:, :, :T] = O.e4m3(rng.standard_normal((1, 16, T, 64)).astype(np.float32) * 60)
     sinv, vo = 3e-4, 0.7
     out = np.empty((T, 1024), np.uint8)
-    O.lib().or_attention(q, k, v, 1, sinv, vo, 128, out)
-    Q, K, V = (O.e4m3_dec(a[0, 3, :T]).astype(np.float32) for a in (q, k, v))
-    S = Q @ K.T
-    m = np.full(T, -1e30, np.float32)
-    l = np.zeros(T, np.float32)
-    acc = np.zeros((T, 64), np.float32)
-    np.seterr(over="ignore", invalid="ignore")   # the rescale factor of rows that keep their max is unused
-    for t0 in range(0, T, 128):
-        s = S[:, t0:t0 + 128]
-        tm = s.max(1)
-        re = tm > m + 8.0 / sinv
-        sc = np.exp2((m - tm) * sinv).astype(np.float32)
-        l = np.where(re, l * sc, l)
-        acc = np.where(re[:, None], acc * sc[:, None], acc)
-        m = np.where(re, tm, m)
-        live = ~(tm < m - 10.0 / sinv)
-        p = np.exp2(s * sinv - (m * sinv)[:, None]).astype(np.float32)
-        p = np.where(live[:, None], p, 0)
-        l = l + p.sum(1)
-        acc = acc + O.e4m3_dec(O.e4m3(p)) @ V[t0:t0 + 128]
-    want = O.e4m3((acc * (vo / l)[:, None]).astype(np.float16).astype(np.float32))
+    O.lib().or_attention(q, k, v, 1, sinv, vo, key_tile, slice_rows, out)
+    want = _attention_numpy(O, q, k, v, sinv, vo, key_tile, slice_rows, 3)
     got = out[:, 3 * 64:4 * 64]
     from tests._gpu import e4m3_ordinal
     d = np.abs(e4m3_ordinal(got) - e4m3_ordinal(want))

@@ -1,0 +1,77 @@
+"""The reference's own FP8 flash attention (flash8<1025>, kern_common.cuh:403-543, compiled from the reference's
+header by oracle/Makefile `ref` into oracle/_ref/) run on the GPU next to the oracle's restatement and this
+library's kernel, on the same inputs: it pins the oracle's attention semantics (64-key tiles, lazy rescale and dead
+tiles decided per 16-row warp slice, E4M3 P, fp16-staged output) to the reference's code, and checks this library's
+kernel against the reference directly.
+
+Differences that remain are floating-point ones: the oracle's exp2 is libm's where both GPU kernels use
+ex2.approx, and each implementation sums scores and l in its own order, so a p or an output on an E4M3 rounding
+boundary can land on either side. The kernels are compared on flat scores (no rescale after the first tile) and on
+peaked ones (lazy rescales and dead tiles in play)."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from tests import _gpu as G
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_SO = os.path.join(ROOT, "oracle", "_ref", "libref_attention.so")
+NIMG, TP, T, D = 2, 1152, 1025, 1024
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.exists(REF_SO):
+        pytest.skip("oracle/_ref/libref_attention.so not built (python -c 'import __graft_entry__ as g; g.build()' "
+                    "where the reference sources are present)")
+    lib = C.CDLL(REF_SO)
+    u8 = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+    lib.ref_attention.restype = C.c_int
+    lib.ref_attention.argtypes = [u8, u8, u8, C.c_int, C.c_int, C.c_float, C.c_float, u8]
+    return lib
+
+
+def _inputs(O, peaked):
+    rng = np.random.default_rng(40 + peaked)
+    sd = 3.0 if peaked else 1.0
+    q = np.zeros((NIMG, 16, TP, 64), np.uint8)
+    k, v = np.zeros_like(q), np.zeros_like(q)
+    q[:, :, :T] = O.e4m3(rng.standard_normal((NIMG, 16, T, 64), dtype=np.float32) * 60 * sd)
+    k[:, :, :T] = O.e4m3(rng.standard_normal((NIMG, 16, T, 64), dtype=np.float32) * 60 * sd)
+    v[:, :, :T] = O.e4m3(rng.standard_normal((NIMG, 16, T, 64), dtype=np.float32) * 100)
+    sinv = (0.8 / 448) * (4.0 / 448)
+    vo = (448 / 3.0) * (3.0 / 448) * 0.9
+    return q, k, v, sinv, vo
+
+
+@pytest.mark.parametrize("peaked", [False, True])
+def test_oracle_attention_matches_reference_kernel(ref, cuda, peaked):
+    from oracle import oracle as O
+    q, k, v, sinv, vo = _inputs(O, peaked)
+    got = np.empty((NIMG * T, D), np.uint8)
+    assert ref.ref_attention(q, k, v, NIMG, TP, sinv, vo, got) == 0
+    want = np.empty((NIMG * T, D), np.uint8)
+    O.lib().or_attention(q, k, v, NIMG, sinv, vo, 64, 16, want)
+    d = np.abs(G.e4m3_ordinal(got) - G.e4m3_ordinal(want))
+    print(f"reference kernel vs oracle: {(d == 0).mean():.5f} identical, max {d.max()} codes apart")
+    G.assert_attention_close(got, want, "reference kernel vs oracle")
+
+
+@pytest.mark.parametrize("peaked", [False, True])
+def test_attention_kernel_matches_reference_kernel(xlib, ref, cuda, peaked):
+    import torch
+    from oracle import oracle as O
+    q, k, v, sinv, vo = _inputs(O, peaked)
+    want = np.empty((NIMG * T, D), np.uint8)
+    assert ref.ref_attention(q, k, v, NIMG, TP, sinv, vo, want) == 0
+    out = G.zeros((NIMG * T, D), torch.uint8)
+    assert xlib.xtb_attention(G.P(G.dev(q)), G.P(G.dev(k)), G.P(G.dev(v)), NIMG, G.P(out), sinv, vo, None) == 0
+    G.check_error_word(xlib)
+    got = G.host(out)
+    d = np.abs(G.e4m3_ordinal(got) - G.e4m3_ordinal(want))
+    print(f"kernel vs reference kernel: {(d == 0).mean():.5f} identical, max {d.max()} codes apart")
+    G.assert_attention_close(got, want, "kernel vs reference kernel")

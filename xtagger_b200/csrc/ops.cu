@@ -179,7 +179,7 @@ int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, 
 int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st)
 {
     if (set_smem((const void *)k_attention, ATT_SMEM)) return -1;
-    dim3 grid(QT, NH, nimg);
+    dim3 grid(ATT_QPAIRS, NH, nimg);
     k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
     XTB_CK(cudaGetLastError());
     return 0;
