@@ -10,17 +10,23 @@
 //     in E4M3; the slice's P is zero and l does not advance;
 //   - P is quantised to E4M3 for the P V product; l sums the unquantised p; out = E4M3(fp16(O * vo / l)).
 //
-// Work split (320 threads, 2 CTAs per SM): one CTA per pair of 128-query tiles of one (head, image); the two tiles
-// ("groups") share every K / V tile. Warp 0 TMA (both Q tiles once; K / V in tiles of 128 keys through a 3-deep
-// ring), warp 1 TMEM allocation (256 columns: S_g at [64 g, 64 g + 64), O_g at [128 + 64 g, 192 + 64 g)) and the MMA
-// issuer, warps 2..5 the softmax of group 0 and warps 6..9 that of group 1, one query row per thread (warp w reads
-// TMEM lanes 32 (w % 4) ..). Per 64-key step u and group g: S_g,u = Q_g K_u^T (M 128, N 64 keys, K 64 dims); the
-// softmax reads it in one pass with the running max (p, l and the tile max together) and re-passes a warp only when
-// one of its slices rescales; it writes P_g,u (128 x 64 E4M3, 64B-swizzled K-major) to shared memory; O_g += P_g,u V_u
-// (M 128, N 64 dims, K 64 keys) accumulates in TMEM with V read as an MN-major operand straight from its
-// [token][64 dims] rows. While one group's softmax works, the tensor core computes the other group's scores, and 16
-// softmax warps per SM (4 per sub-partition) keep the exp2 unit fed through each warp's latencies. Warps whose 32
-// query rows are all padding (the last query tile holds one real row) skip the math.
+// Work split (320 threads, 2 CTAs per SM): one CTA per pair of 128-query tiles of one (head, image) covering rows
+// 0 .. 1023; the two tiles ("groups") share every K / V tile. Warp 0 TMA (both Q tiles once; K / V in tiles of 128
+// keys through a 3-deep ring), warp 1 TMEM allocation (256 columns: S_g at [64 g, 64 g + 64), O_g at
+// [128 + 64 g, 192 + 64 g)) and the MMA issuer, warps 2..5 the softmax of group 0 and warps 6..9 that of group 1, one
+// query row per thread (warp w reads TMEM lanes 32 (w % 4) ..). Per 64-key step u and group g: S_g,u = Q_g K_u^T
+// (M 128, N 64 keys, K 64 dims); the softmax reads it in one pass with the running max (p, l and the tile max
+// together) and re-passes a warp only when one of its slices rescales; it writes P_g,u (128 x 64 E4M3, 64B-swizzled
+// K-major) to shared memory; O_g += P_g,u V_u (M 128, N 64 dims, K 64 keys) accumulates in TMEM with V read as an
+// MN-major operand straight from its [token][64 dims] rows. While one group's softmax works, the tensor core
+// computes the other group's scores, and 16 softmax warps per SM (4 per sub-partition) keep the exp2 unit fed
+// through each warp's latencies.
+//
+// Query row 1024 (the last token) is the only real row of its 128-row tile; a CTA for it would run all 17 steps for
+// one row. k_attention_last computes it instead, one warp per (head, image). Its reference slice (rows 1024 .. 1039)
+// holds 15 zero query rows of the padding, whose scores are all 0: they never ask for a rescale after the first
+// tile and never let the slice go dead, so the row follows the per-row rule (rescale when its own tile max exceeds
+// m + RESCALE / sinv; no dead tiles), which the warp applies exactly.
 #pragma once
 #include "ops.h"
 #include "ptx.cuh"
@@ -34,7 +40,8 @@ constexpr int ATT_NSUB = (T + ATT_SUB - 1) / ATT_SUB;  // 17 steps; the last hol
 constexpr int ATT_NK = (ATT_NSUB + 1) / 2;        // 9 K / V tiles of 128 keys
 constexpr int ATT_KS = 3;                         // K / V ring depth (128-key tiles)
 constexpr int ATT_G = 2;                          // query tiles (groups) per CTA
-constexpr int ATT_QPAIRS = (QT + ATT_G - 1) / ATT_G;  // CTAs per (head, image)
+constexpr int ATT_QTF = (T - 1) / 128;               // full query tiles (8): rows 0 .. 1023
+constexpr int ATT_QPAIRS = ATT_QTF / ATT_G;           // CTAs per (head, image); row 1024 goes to k_attention_last
 constexpr int ATT_PB = 2;                         // P buffers per group in shared memory
 constexpr int ATT_THREADS = 64 + 32 * 4 * ATT_G;
 constexpr int ATT_Q_BYTES = 128 * 64;
@@ -54,26 +61,26 @@ __device__ __forceinline__ float ex2(float x)
 // 16-byte chunk q (0..3) of row r of a P buffer: 64-byte rows, 64B swizzle (the layout the MMA descriptor reads)
 __device__ __forceinline__ uint8_t *p_chunk(uint8_t *prow, int r, int q) { return prow + ((q ^ ((r >> 1) & 3)) << 4); }
 
-// Max of a row's valid scores in an S buffer (TMEM, 64 columns at sS).
-__device__ __forceinline__ float tile_max(uint32_t sS, int nvalid)
+// Max of a row's scores in a full S buffer (TMEM, 64 columns at sS).
+__device__ __forceinline__ float tile_max(uint32_t sS)
 {
     float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int c = 0; c < 2; c++) {
-        if (c * 32 < nvalid) {  // warp-uniform
-            float v[32];
-            tmem_ld32(sS + c * 32, v);
-            tmem_wait_ld();
+        float v[32];
+        tmem_ld32(sS + c * 32, v);
+        tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; i++)
-                if (nvalid == 64 || c * 32 + i < nvalid) t4[i & 3] = fmaxf(t4[i & 3], v[i]);
-        }
+        for (int i = 0; i < 32; i += 8)
+#pragma unroll
+            for (int e = 0; e < 4; e++) t4[e] = fmax3(t4[e], v[i + 2 * e], v[i + 2 * e + 1]);
     }
     return fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
 }
 
 // One pass over a row of an S buffer with max m: tile max, p = exp2(s sinv - m sinv), sum of p, E4M3(p) -> the
-// row of P. Masked keys give p = 0.
+// row of P. FULL: all 64 keys are valid (every step but the last); otherwise keys >= nvalid are masked (p = 0).
+template <bool FULL>
 __device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int nvalid, float2 sv2, float m, float *tm_out,
                                          float *l_out)
 {
@@ -83,22 +90,22 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int 
 #pragma unroll
     for (int c = 0; c < 2; c++) {
         uint32_t w[8];
-        if (c * 32 < nvalid) {  // warp-uniform
+        if (FULL || c * 32 < nvalid) {  // warp-uniform
             float v[32];
             tmem_ld32(sS + c * 32, v);
             tmem_wait_ld();
-            if (nvalid < 64) {
+            if (!FULL) {
 #pragma unroll
                 for (int i = 0; i < 32; i++)
                     if (c * 32 + i >= nvalid) v[i] = -INFINITY;
             }
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
+                t4[(i >> 2) & 1] = fmax3(t4[(i >> 2) & 1], v[i], v[i + 1]);
+                t4[2 + ((i >> 2) & 1)] = fmax3(t4[2 + ((i >> 2) & 1)], v[i + 2], v[i + 3]);
                 float pp[4];
 #pragma unroll
                 for (int e = 0; e < 4; e += 2) {
-                    t4[e] = fmaxf(t4[e], v[i + e]);
-                    t4[e + 1] = fmaxf(t4[e + 1], v[i + e + 1]);
                     const float2 a = fma2(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
                     pp[e] = ex2(a.x);
                     pp[e + 1] = ex2(a.y);
@@ -152,7 +159,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt0 = blockIdx.x * ATT_G, h = blockIdx.y, b = blockIdx.z;
-    const int ng = min(ATT_G, QT - qt0);                 // query tiles this CTA holds
+    constexpr int ng = ATT_G;                            // query tiles this CTA holds
     const int bh = b * NH + h;
 
     if (threadIdx.x == 0) {
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                 }
             }
         }
-    } else if ((warp - 2) / 4 < ng) {
+    } else {
         const int g = (warp - 2) / 4;                    // query tile (group) of this warp
         const int quad = warp & 3;
         const int r = quad * 32 + lane;                  // query row within the tile = TMEM lane
@@ -248,7 +255,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         const uint32_t sS = tbase + g * 64 + lrow, sO = tbase + 128 + g * 64 + lrow;
         uint64_t *gp_full = p_full + g * ATT_PB, *gpv_done = pv_done + g * ATT_PB;
         const float thr = ATT_RESCALE / sinv, dthr = ATT_PSKIP / sinv;
-        const bool idle = (qt0 + g) * 128 + quad * 32 >= T;   // warp-uniform: every row of the warp is padding
         const uint32_t half = lane < 16 ? 0x0000FFFFu : 0xFFFF0000u;  // this row's 16-row slice
         const float2 sv2 = make_float2(sinv, sinv);
         float m = -1e30f, l = 0.f;
@@ -263,13 +269,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                 !(ok = __all_sync(0xffffffffu, mbar_wait(&gpv_done[pb], ((u >> 1) - 1) & 1, err, XTB_ERR_WAIT_ATTN))))
                 break;
             tc_fence_after();
-            if (idle) {
-                zero_prow(prow);
-            } else {
+            {
                 // one pass with the running max: tile max, p = exp2(s sinv - m sinv), l_tile, P
                 float tm = -INFINITY, lt = 0.f;
-                if (u > 0) exp_pass(sS, prow, r, nvalid, sv2, m, &tm, &lt);
-                else tm = tile_max(sS, nvalid);
+                const bool full = u < ATT_NSUB - 1;     // the last step holds one key
+                if (u == 0) tm = tile_max(sS);
+                else if (full) exp_pass<true>(sS, prow, r, nvalid, sv2, m, &tm, &lt);
+                else exp_pass<false>(sS, prow, r, nvalid, sv2, m, &tm, &lt);
                 const float mn = fmaxf(m, tm);
                 const bool resc = (__ballot_sync(0xffffffffu, mn > m + thr) & half) != 0;
                 if (__any_sync(0xffffffffu, resc)) {
@@ -300,7 +306,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                     }
                     // (re)compute P with the refreshed max; the other slice recomputes the same values
                     float tm2;
-                    exp_pass(sS, prow, r, nvalid, sv2, m, &tm2, &lt);
+                    if (full) exp_pass<true>(sS, prow, r, nvalid, sv2, m, &tm2, &lt);
+                    else exp_pass<false>(sS, prow, r, nvalid, sv2, m, &tm2, &lt);
                 }
                 if ((__ballot_sync(0xffffffffu, tm < m - dthr) & half) == half) {  // dead slice: P zero, l unchanged
                     zero_prow(prow);
@@ -321,7 +328,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             const int wl = ATT_NSUB - 1;
             ok = __all_sync(0xffffffffu, mbar_wait(&gpv_done[wl & 1], (wl >> 1) & 1, err, XTB_ERR_WAIT_ATTN));
         }
-        if (ok && !idle) {
+        if (ok) {
             tc_fence_after();
             const float f = vo / l;
             uint32_t w[16];
@@ -335,11 +342,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                     w[c * 8 + (i >> 2)] = e4m3x2_via_f16(v[i] * f, v[i + 1] * f) | (e4m3x2_via_f16(v[i + 2] * f, v[i + 3] * f) << 16);
             }
             const int t = (qt0 + g) * 128 + r;
-            if (t < T) {
-                uint4 *o = (uint4 *)(out + ((size_t)b * T + t) * D + h * HD);
+            uint4 *o = (uint4 *)(out + ((size_t)b * T + t) * D + h * HD);
 #pragma unroll
-                for (int c = 0; c < 4; c++) o[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-            }
+            for (int c = 0; c < 4; c++) o[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
         }
     }
     __syncthreads();
@@ -347,6 +352,146 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tbase, 256);
+    }
+}
+
+
+// Query row 1024 of every (head, image): one CTA of 256 threads each, in parallel over keys instead of a sequential
+// walk over the 17 key tiles. The walk only matters through the running max, and for a single row it is a scan over
+// the 17 tile maxima: m_u, the max in force while tile u is accumulated (m_u = tm_u when tm_u > m_{u-1} + RESCALE /
+// sinv, else m_{u-1}; m_0 = tm_0), and the factor w_u = prod of exp2((m_{v-1} - m_v) sinv) over the later rescales
+// v > u that the reference applies to l and O after tile u. Then p_k = exp2(s_k sinv - m_u sinv) (one fma, ex2.approx),
+// l = sum_u w_u sum_{k in u} p_k and O = sum_u w_u sum_{k in u} E4M3(p_k) V_k: the reference's values, summed in
+// another order.
+constexpr int ATT_LAST_THREADS = 256;
+
+__device__ __forceinline__ void e4m3x4_to_f32(uint32_t w, float *f)
+{
+    const float2 a = __half22float2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xffff), __NV_E4M3));
+    const float2 b = __half22float2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w >> 16), __NV_E4M3));
+    f[0] = a.x;
+    f[1] = a.y;
+    f[2] = b.x;
+    f[3] = b.y;
+}
+
+__global__ void __launch_bounds__(ATT_LAST_THREADS)
+    k_attention_last(const uint8_t *__restrict__ q8, const uint8_t *__restrict__ k8, const uint8_t *__restrict__ v8,
+                     uint8_t *__restrict__ out, float sinv, float vo)
+{
+    __shared__ float sq[64];
+    __shared__ float ss[ATT_NSUB * 64];          // scores, then E4M3-rounded p (keys >= 1025: 0)
+    __shared__ float stm[ATT_NSUB], sm_u[ATT_NSUB], sw[ATT_NSUB], sl[ATT_NSUB];
+    __shared__ float2 sop[8][32];                // O partial sums: [key quarter x tile parity][dim pair]
+    const int bh = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t = T - 1;
+    const size_t base = (size_t)bh * TP;
+    if (tid < 16) {
+        float f[4];
+        e4m3x4_to_f32(__ldg((const uint32_t *)(q8 + (base + t) * 64) + tid), f);
+#pragma unroll
+        for (int x = 0; x < 4; x++) sq[4 * tid + x] = f[x];
+    }
+    __syncthreads();
+    // scores: keys tid, tid + 256, ...; four partial sums per dot product
+    for (int key = tid; key < ATT_NSUB * 64; key += ATT_LAST_THREADS) {
+        float sc = -INFINITY;
+        if (key < T) {
+            const uint4 *kr = (const uint4 *)(k8 + (base + key) * 64);
+            float a4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const uint4 w = __ldg(kr + c);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float kf[4];
+                    e4m3x4_to_f32(ws[e], kf);
+#pragma unroll
+                    for (int x = 0; x < 4; x++) a4[x] = fmaf(sq[16 * c + 4 * e + x], kf[x], a4[x]);
+                }
+            }
+            sc = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+        }
+        ss[key] = sc;
+    }
+    __syncthreads();
+    // tile maxima: warp w takes tiles w, w + 8, ...
+    for (int u = warp; u < ATT_NSUB; u += ATT_LAST_THREADS / 32) {
+        float tm = fmaxf(ss[u * 64 + lane], ss[u * 64 + 32 + lane]);
+#pragma unroll
+        for (int sh = 16; sh; sh >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, sh));
+        if (lane == 0) stm[u] = tm;
+    }
+    __syncthreads();
+    if (tid == 0) {  // the running max of the reference's walk, and the rescale factors applied after each tile
+        const float thr = ATT_RESCALE / sinv;
+        float m = -1e30f;
+        for (int u = 0; u < ATT_NSUB; u++) {
+            const float tm = stm[u];
+            float sc = 1.0f;
+            if (tm > m + thr) {
+                sc = ex2((m - tm) * sinv);
+                m = tm;
+            }
+            sm_u[u] = m;
+            sw[u] = sc;  // factor applied to l and O when tile u starts
+        }
+        float w = 1.0f;  // suffix products: w_u = product of the factors of the tiles after u
+        for (int u = ATT_NSUB - 1; u >= 0; u--) {
+            const float sc = sw[u];
+            sw[u] = w;
+            w *= sc;
+        }
+    }
+    __syncthreads();
+    // p, per-tile sums of p (warp w: tiles w, w + 8, ...), E4M3-rounded p back into ss
+    for (int u = warp; u < ATT_NSUB; u += ATT_LAST_THREADS / 32) {
+        const float nm = -sm_u[u] * sinv;
+        float lp = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            const int key = u * 64 + hh * 32 + lane;
+            const float p = ex2(fmaf(ss[key], sinv, nm));  // masked keys: exp2(-inf) = 0
+            lp += p;
+            ss[key] = __low2float(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)e4m3x2(p, 0.f), __NV_E4M3));
+        }
+#pragma unroll
+        for (int sh = 16; sh; sh >>= 1) lp += __shfl_xor_sync(0xffffffffu, lp, sh);
+        if (lane == 0) sl[u] = lp;
+    }
+    __syncthreads();
+    // O: thread = (dim pair, key quarter); tile weights applied per tile
+    {
+        const int dp = tid & 31, qk = tid >> 5;   // dims 2 dp, 2 dp + 1; keys of quarter qk % 4 in tiles (qk / 4) ...
+        float o0 = 0.f, o1 = 0.f;
+        for (int u = qk >> 2; u < ATT_NSUB; u += 2) {
+            const int k0 = u * 64 + (qk & 3) * 16, k1 = min(k0 + 16, T);
+            float a0 = 0.f, a1 = 0.f;
+            for (int key = k0; key < k1; key++) {
+                const float pq = ss[key];
+                const uint32_t vv = __ldg((const unsigned short *)(v8 + (base + key) * 64) + dp);
+                const float2 vf = __half22float2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)vv, __NV_E4M3));
+                a0 = fmaf(pq, vf.x, a0);
+                a1 = fmaf(pq, vf.y, a1);
+            }
+            o0 = fmaf(sw[u], a0, o0);
+            o1 = fmaf(sw[u], a1, o1);
+        }
+        // 8 partial sums per dim pair (qk = 0..7) -> shared memory, then thread qk = 0 adds them
+        sop[qk][dp] = make_float2(o0, o1);
+        __syncthreads();
+        if (qk == 0) {
+            float2 acc = sop[0][dp];
+#pragma unroll
+            for (int i = 1; i < 8; i++) acc = make_float2(acc.x + sop[i][dp].x, acc.y + sop[i][dp].y);
+            float l = 0.f;
+            for (int u = 0; u < ATT_NSUB; u++) l = fmaf(sw[u], sl[u], l);
+            const float f = vo / l;
+            const int img = bh / NH, h = bh % NH;
+            *(unsigned short *)(out + ((size_t)img * T + t) * D + h * HD + 2 * dp) =
+                (unsigned short)e4m3x2_via_f16(acc.x * f, acc.y * f);
+        }
     }
 }
 

@@ -2,7 +2,7 @@
 //
 // Bring-up (eva_open / eva_open_ex -> boot thread): read the weight file (v3 per-tensor or v4 block-scaled) into
 // pinned host memory, copy it to every device, resolve the tensor layout, allocate the activations for the
-// device's batch, build the TMA descriptors, capture the whole forward (172 launches) into one CUDA graph per
+// device's batch, build the TMA descriptors, capture the whole forward (220 launches) into one CUDA graph per
 // device. Per batch (eva_submit): H2D of the inputs (adjacent pool inputs in one copy), graph launch, D2H of the
 // scores (and head inputs), event; eva_wait sleeps on the events. Multi-GPU: one replica per device with its own
 // stream and graph; a submit's inputs are split into contiguous shards, one per device, and the scores land in
@@ -279,7 +279,7 @@ int forward(Impl *im, Replica &r, eva *e, Prof *p)
         RCK(record(p, st, P_FC1));
         RCK(launch_fc2(r.op_h8, L.w[3], L.adq[3], rows, r.x, r.stat, L.c, L.d, st));
         RCK(record(p, st, P_FC2));
-        n += 7;
+        n += 9;  // ln1, qkv, attention (2), oproj, ln2, fc1, fc2 (row statistics + GEMM)
     }
     RCK(launch_pool_ln(r.x, nb, r.fnw, r.fnb, r.pool, r.pn, im->head8 ? r.pn8 : nullptr, 1.0f / im->head_adq, st));
     n += 2;

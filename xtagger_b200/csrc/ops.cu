@@ -170,6 +170,9 @@ int launch_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, uint8
 int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg)
 {
     const uint64_t rows = (uint64_t)nimg * NH * TP;
+    a->q8 = q8;
+    a->k8 = k8;
+    a->v8 = v8;
     if (make_tmap_2d(&a->tq, q8, HD, rows, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     if (make_tmap_2d(&a->tk, k8, HD, rows, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     if (make_tmap_2d(&a->tv, v8, HD, rows, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
@@ -181,6 +184,8 @@ int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo
     if (set_smem((const void *)k_attention, ATT_SMEM)) return -1;
     dim3 grid(ATT_QPAIRS, NH, nimg);
     k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
+    XTB_CK(cudaGetLastError());
+    k_attention_last<<<nimg * NH, ATT_LAST_THREADS, 0, st>>>(a.q8, a.k8, a.v8, out, sinv, vo);
     XTB_CK(cudaGetLastError());
     return 0;
 }

@@ -40,6 +40,7 @@ struct Weight8 {
 
 struct Attn {
     CUtensorMap tq, tk, tv;
+    const uint8_t *q8, *k8, *v8;
 };
 
 // ---- launchers (device pointers; stream-ordered) ----

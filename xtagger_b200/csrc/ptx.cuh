@@ -368,6 +368,14 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b)
     return bits_f2(d);
 }
 
+// max(a, b, c) in one instruction (three-operand max.f32, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll
