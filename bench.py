@@ -33,6 +33,9 @@ METRIC = "images/sec EVA02-L 448² (1/2/4/8 B200) + FP8 GEMM % of tensor peak"
 NT = 10861
 MODEL_KW = dict(seed=0, nt=NT, nl=24, version=4, head_fp8=True)
 FC1_FLOP_PER_ROW = 2.0 * 5472 * 1024
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one fc1 launch in an ncu capture at batch 32
+# (32 x 1025 rows): 39.34 MB + 47.44 MB; the launch at another batch is scaled by the rows it processes.
+FC1_TRAFFIC_PER_ROW = (39.344128e6 + 47.437312e6) / (32 * 1025)
 FLOP_PER_IMAGE = 723.5e9
 
 
@@ -236,7 +239,8 @@ def run_ours(args, rank, world, local):
                 "roofline": {"bound": "tensor", "kernel": "fc1 (tcgen05 E4M3 GEMM + SwiGLU epilogue)",
                              "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                              "peak_source": peak_src, "flop_per_launch": FC1_FLOP_PER_ROW * rows,
-                             "launch_ms": fc1_ms, "traffic": None},
+                             "launch_ms": fc1_ms, "traffic": FC1_TRAFFIC_PER_ROW * rows,
+                             "traffic_unit": "bytes per launch (ncu DRAM read + write at batch 32, scaled by rows)"},
                 "forward_tflops": FLOP_PER_IMAGE * value / 1e12,
                 "profile_ms": prof,
                 "clocks": clocks,
