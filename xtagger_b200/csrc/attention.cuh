@@ -16,11 +16,12 @@
 // [128 + 64 g, 192 + 64 g)) and the MMA issuer, warps 2..5 the softmax of group 0 and warps 6..9 that of group 1, one
 // query row per thread (warp w reads TMEM lanes 32 (w % 4) ..). Per 64-key step u and group g: S_g,u = Q_g K_u^T
 // (M 128, N 64 keys, K 64 dims); the softmax reads it in one pass with the running max (p, l and the tile max
-// together) and re-passes a warp only when one of its slices rescales; it writes P_g,u (128 x 64 E4M3, 64B-swizzled
-// K-major) to shared memory; O_g += P_g,u V_u (M 128, N 64 dims, K 64 keys) accumulates in TMEM with V read as an
-// MN-major operand straight from its [token][64 dims] rows. While one group's softmax works, the tensor core
-// computes the other group's scores, and 16 softmax warps per SM (4 per sub-partition) keep the exp2 unit fed
-// through each warp's latencies.
+// together) and re-passes a warp only when one of its slices rescales; it writes P_g,u (the row's 64 E4M3 values)
+// with one tcgen05.st into the first 16 columns of S_g, where O_g += P_g,u V_u (M 128, N 64 dims, K 64 keys) reads it
+// as a TMEM A operand, V being an MN-major operand straight from its [token][64 dims] rows. The MMA issues PV_g,u
+// before S_g,u+1, which overwrites those columns; the tensor core keeps the order, so the commit that signals
+// S_g,u+1 also means PV_g,u is done. While one group's softmax works, the tensor core computes the other group's
+// scores, and 16 softmax warps per SM (4 per sub-partition) keep the exp2 unit fed through each warp's latencies.
 //
 // Query row 1024 (the last token) is the only real row of its 128-row tile; a CTA for it would run all 17 steps for
 // one row. k_attention_last computes it instead, one warp per (head, image). Its reference slice (rows 1024 .. 1039)
@@ -42,14 +43,11 @@ constexpr int ATT_KS = 3;                         // K / V ring depth (128-key t
 constexpr int ATT_G = 2;                          // query tiles (groups) per CTA
 constexpr int ATT_QTF = (T - 1) / 128;               // full query tiles (8): rows 0 .. 1023
 constexpr int ATT_QPAIRS = ATT_QTF / ATT_G;           // CTAs per (head, image); row 1024 goes to k_attention_last
-constexpr int ATT_PB = 2;                         // P buffers per group in shared memory
 constexpr int ATT_THREADS = 64 + 32 * 4 * ATT_G;
 constexpr int ATT_Q_BYTES = 128 * 64;
 constexpr int ATT_K_BYTES = 128 * 64;
 constexpr int ATT_V_BYTES = 128 * 64;
-constexpr int ATT_P_BYTES = 128 * 64;             // 128 rows x 64 keys
-constexpr size_t ATT_SMEM =
-    1024 + ATT_G * ATT_Q_BYTES + ATT_KS * (ATT_K_BYTES + ATT_V_BYTES) + ATT_G * ATT_PB * ATT_P_BYTES + 512;
+constexpr size_t ATT_SMEM = 1024 + ATT_G * ATT_Q_BYTES + ATT_KS * (ATT_K_BYTES + ATT_V_BYTES) + 512;
 
 __device__ __forceinline__ float ex2(float x)
 {
@@ -58,8 +56,6 @@ __device__ __forceinline__ float ex2(float x)
     return y;
 }
 
-// 16-byte chunk q (0..3) of row r of a P buffer: 64-byte rows, 64B swizzle (the layout the MMA descriptor reads)
-__device__ __forceinline__ uint8_t *p_chunk(uint8_t *prow, int r, int q) { return prow + ((q ^ ((r >> 1) & 3)) << 4); }
 
 // Max of a row's scores in a full S buffer (TMEM, 64 columns at sS).
 __device__ __forceinline__ float tile_max(uint32_t sS)
@@ -81,7 +77,7 @@ __device__ __forceinline__ float tile_max(uint32_t sS)
 // One pass over a row of an S buffer with max m: tile max, p = exp2(s sinv - m sinv), sum of p, E4M3(p) -> the
 // row of P. FULL: all 64 keys are valid (every step but the last); otherwise keys >= nvalid are masked (p = 0).
 template <bool FULL>
-__device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int nvalid, float2 sv2, float m, float *tm_out,
+__device__ __forceinline__ void exp_pass(uint32_t sS, uint32_t *w, int nvalid, float2 sv2, float m, float *tm_out,
                                          float *l_out)
 {
     const float2 nm2 = make_float2(-m * sv2.x, -m * sv2.x);
@@ -89,7 +85,6 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int 
     float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
     for (int c = 0; c < 2; c++) {
-        uint32_t w[8];
         if (FULL || c * 32 < nvalid) {  // warp-uniform
             float v[32];
             tmem_ld32(sS + c * 32, v);
@@ -111,23 +106,15 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint8_t *prow, int r, int 
                     pp[e + 1] = ex2(a.y);
                     l2[e >> 1] = add2(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
                 }
-                w[i >> 2] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
+                w[c * 8 + (i >> 2)] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
             }
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; i++) w[i] = 0;
+            for (int i = 0; i < 8; i++) w[c * 8 + i] = 0;
         }
-        *(uint4 *)p_chunk(prow, r, 2 * c) = make_uint4(w[0], w[1], w[2], w[3]);
-        *(uint4 *)p_chunk(prow, r, 2 * c + 1) = make_uint4(w[4], w[5], w[6], w[7]);
     }
     *tm_out = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
     *l_out = (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
-}
-
-__device__ __forceinline__ void zero_prow(uint8_t *prow)
-{
-#pragma unroll
-    for (int q = 0; q < 4; q++) *(uint4 *)(prow + 16 * q) = make_uint4(0, 0, 0, 0);
 }
 
 // fp32 -> fp16 (round to nearest) -> E4M3, as the reference's output staging (kern_common.cuh:527-541)
@@ -146,16 +133,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     uint8_t *sQ = smem;                                  // [ATT_G]
     uint8_t *sK = sQ + ATT_G * ATT_Q_BYTES;              // [ATT_KS]
     uint8_t *sV = sK + ATT_KS * ATT_K_BYTES;             // [ATT_KS]
-    uint8_t *sP = sV + ATT_KS * ATT_V_BYTES;             // [ATT_G][ATT_PB]
-    uint64_t *bar = (uint64_t *)(sP + ATT_G * ATT_PB * ATT_P_BYTES);
+    uint64_t *bar = (uint64_t *)(sV + ATT_KS * ATT_V_BYTES);
     uint64_t *q_full = bar;
     uint64_t *kv_full = q_full + 1;                      // [ATT_KS]
     uint64_t *kv_empty = kv_full + ATT_KS;               // [ATT_KS]
-    uint64_t *s_full = kv_empty + ATT_KS;                // [ATT_G]
-    uint64_t *s_free = s_full + ATT_G;                   // [ATT_G]
-    uint64_t *p_full = s_free + ATT_G;                   // [ATT_G][ATT_PB]
-    uint64_t *pv_done = p_full + ATT_G * ATT_PB;         // [ATT_G][ATT_PB]
-    uint32_t *tslot = (uint32_t *)(pv_done + ATT_G * ATT_PB);
+    uint64_t *s_full = kv_empty + ATT_KS;                // [ATT_G] S_g,u in TMEM (and every earlier MMA done)
+    uint64_t *p_full = s_full + ATT_G;                   // [ATT_G] softmax g has read S_g,u and written P_g,u
+    uint64_t *pv_done = p_full + ATT_G;                  // [ATT_G] PV_g,u done
+    uint32_t *tslot = (uint32_t *)(pv_done + ATT_G);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt0 = blockIdx.x * ATT_G, h = blockIdx.y, b = blockIdx.z;
@@ -170,11 +155,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         }
         for (int g = 0; g < ATT_G; g++) {
             mbar_init(&s_full[g], 1);
-            mbar_init(&s_free[g], 4);
-            for (int s = 0; s < ATT_PB; s++) {
-                mbar_init(&p_full[g * ATT_PB + s], 4);
-                mbar_init(&pv_done[g * ATT_PB + s], 1);
-            }
+            mbar_init(&p_full[g], 4);
+            mbar_init(&pv_done[g], 1);
         }
         fence_mbar_init();
         tma_prefetch_desc(&tq);
@@ -209,42 +191,37 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         }
     } else if (warp == 1) {
         if (elect_one()) {
-            // S: N = 64 keys. PV: B = V, MN-major (bit 16): its N (dims) run contiguous within each key's 64-byte row
+            // S: N = 64 keys. PV: A = P from TMEM (16 columns of the group's S buffer), B = V, MN-major (bit 16)
             constexpr uint32_t ID_S = idesc_m128(64), ID_PV = idesc_m128(64) | (1u << 16);
             bool ok = mbar_wait(q_full, 0, err, XTB_ERR_WAIT_ATTN);
             for (int u = 0; u <= ATT_NSUB && ok; u++) {
-                if (u < ATT_NSUB) {  // S_g,u = Q_g K_u^T, each group once its softmax has read S_g,u-1
-                    const int j = u >> 1, st = j % ATT_KS;
-                    if (!(u & 1) && !(ok = mbar_wait(&kv_full[st], (j / ATT_KS) & 1, err, XTB_ERR_WAIT_ATTN))) break;
-                    const uint32_t k0 = smem_u32(sK + st * ATT_K_BYTES) + (u & 1) * 4096;  // 64 keys x 64 bytes in
-                    for (int g = 0; g < ng && ok; g++) {
-                        if (u > 0 && !(ok = mbar_wait(&s_free[g], (u - 1) & 1, err, XTB_ERR_WAIT_ATTN))) break;
+                const int j = u >> 1, st = j % ATT_KS;
+                if (u < ATT_NSUB && !(u & 1) && !(ok = mbar_wait(&kv_full[st], (j / ATT_KS) & 1, err, XTB_ERR_WAIT_ATTN)))
+                    break;
+                const int w = u - 1, wst = (w >> 1) % ATT_KS;
+                for (int g = 0; g < ng && ok; g++) {
+                    const uint32_t tS = tbase + g * 64;
+                    if (u > 0) {  // O_g += P_g,w V_w; P lives in S_g's first 16 columns until S_g,u overwrites them
+                        if (!(ok = mbar_wait(&p_full[g], w & 1, err, XTB_ERR_WAIT_ATTN))) break;
                         tc_fence_after();
-                        const uint32_t q0 = smem_u32(sQ + g * ATT_Q_BYTES);
+                        const uint32_t v0 = smem_u32(sV + wst * ATT_V_BYTES) + (w & 1) * 4096;
 #pragma unroll
                         for (int kk = 0; kk < 2; kk++)
-                            umma<false>(tbase + g * 64, sdesc(q0 + kk * 32, 512, SWZ_64B), sdesc(k0 + kk * 32, 512, SWZ_64B),
-                                        ID_S, kk);
+                            umma_tmem_a(tbase + 128 + g * 64, tS + kk * 8, sdesc_mn(v0 + kk * 2048, 512, SWZ_64B), ID_PV,
+                                        (w > 0 || kk > 0));
+                        umma_commit(&pv_done[g]);
+                    }
+                    if (u < ATT_NSUB) {  // S_g,u = Q_g K_u^T, issued after PV_g,w (the tensor core keeps the order)
+                        const uint32_t q0 = smem_u32(sQ + g * ATT_Q_BYTES);
+                        const uint32_t k0 = smem_u32(sK + st * ATT_K_BYTES) + (u & 1) * 4096;
+#pragma unroll
+                        for (int kk = 0; kk < 2; kk++)
+                            umma<false>(tS, sdesc(q0 + kk * 32, 512, SWZ_64B), sdesc(k0 + kk * 32, 512, SWZ_64B), ID_S, kk);
                         umma_commit(&s_full[g]);
                     }
-                    if (!ok) break;
                 }
-                if (u > 0) {  // O_g += P_g,w V_w for the previous step
-                    const int w = u - 1, pb = w & 1, st = (w >> 1) % ATT_KS;
-                    const uint32_t v0 = smem_u32(sV + st * ATT_V_BYTES) + (w & 1) * 4096;
-                    for (int g = 0; g < ng && ok; g++) {
-                        if (!(ok = mbar_wait(&p_full[g * ATT_PB + pb], (w >> 1) & 1, err, XTB_ERR_WAIT_ATTN))) break;
-                        tc_fence_after();
-                        const uint32_t p0 = smem_u32(sP + (g * ATT_PB + pb) * ATT_P_BYTES);
-#pragma unroll
-                        for (int kk = 0; kk < 2; kk++)
-                            umma<false>(tbase + 128 + g * 64, sdesc(p0 + kk * 32, 512, SWZ_64B),
-                                        sdesc_mn(v0 + kk * 2048, 512, SWZ_64B), ID_PV, (w > 0 || kk > 0));
-                        umma_commit(&pv_done[g * ATT_PB + pb]);
-                    }
-                    if (!ok) break;
-                    if ((w & 1) || w == ATT_NSUB - 1) umma_commit(&kv_empty[st]);  // the K / V tile is used up
-                }
+                if (!ok) break;
+                if (u > 0 && ((w & 1) || w == ATT_NSUB - 1)) umma_commit(&kv_empty[wst]);  // the K / V tile is used up
             }
         }
     } else {
@@ -253,81 +230,64 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         const int r = quad * 32 + lane;                  // query row within the tile = TMEM lane
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
         const uint32_t sS = tbase + g * 64 + lrow, sO = tbase + 128 + g * 64 + lrow;
-        uint64_t *gp_full = p_full + g * ATT_PB, *gpv_done = pv_done + g * ATT_PB;
         const float thr = ATT_RESCALE / sinv, dthr = ATT_PSKIP / sinv;
         const uint32_t half = lane < 16 ? 0x0000FFFFu : 0xFFFF0000u;  // this row's 16-row slice
         const float2 sv2 = make_float2(sinv, sinv);
         float m = -1e30f, l = 0.f;
         bool ok = true;
         for (int u = 0; u < ATT_NSUB && ok; u++) {
-            const int pb = u & 1;
             const int nvalid = min(ATT_SUB, T - u * ATT_SUB);
-            uint8_t *prow = sP + (g * ATT_PB + pb) * ATT_P_BYTES + r * 64;
+            // S_g,u has landed, and with it every earlier MMA of the CTA (PV_g,u-1 included)
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[g], u & 1, err, XTB_ERR_WAIT_ATTN)))) break;
-            // P buffer pb was last read by PV_{u-2}
-            if (u >= ATT_PB &&
-                !(ok = __all_sync(0xffffffffu, mbar_wait(&gpv_done[pb], ((u >> 1) - 1) & 1, err, XTB_ERR_WAIT_ATTN))))
-                break;
             tc_fence_after();
-            {
-                // one pass with the running max: tile max, p = exp2(s sinv - m sinv), l_tile, P
-                float tm = -INFINITY, lt = 0.f;
-                const bool full = u < ATT_NSUB - 1;     // the last step holds one key
-                if (u == 0) tm = tile_max(sS);
-                else if (full) exp_pass<true>(sS, prow, r, nvalid, sv2, m, &tm, &lt);
-                else exp_pass<false>(sS, prow, r, nvalid, sv2, m, &tm, &lt);
-                const float mn = fmaxf(m, tm);
-                const bool resc = (__ballot_sync(0xffffffffu, mn > m + thr) & half) != 0;
-                if (__any_sync(0xffffffffu, resc)) {
-                    float sc = 1.0f;
-                    if (resc) {  // every row of a rescaling slice takes its max
-                        sc = ex2((m - mn) * sinv);
-                        l *= sc;
-                        m = mn;
-                    }
-                    if (u > 0) {
-                        // O holds P V of the earlier steps: rescale it in TMEM once PV_{u-1} has landed (TMEM access
-                        // is warp-collective: factor 1 for the slice that keeps its max)
-                        const int w = u - 1;
-                        if (!(ok = __all_sync(0xffffffffu,
-                                              mbar_wait(&gpv_done[w & 1], (w >> 1) & 1, err, XTB_ERR_WAIT_ATTN))))
-                            break;
-                        tc_fence_after();
-#pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            float v[16];
-                            tmem_ld16(sO + c * 16, v);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 16; i++) v[i] *= sc;
-                            tmem_st16(sO + c * 16, v);
-                        }
-                        tmem_wait_st();
-                    }
-                    // (re)compute P with the refreshed max; the other slice recomputes the same values
-                    float tm2;
-                    if (full) exp_pass<true>(sS, prow, r, nvalid, sv2, m, &tm2, &lt);
-                    else exp_pass<false>(sS, prow, r, nvalid, sv2, m, &tm2, &lt);
+            uint32_t pw[16];
+            // one pass with the running max: tile max, p = exp2(s sinv - m sinv), l_tile, P
+            float tm = -INFINITY, lt = 0.f;
+            const bool full = u < ATT_NSUB - 1;          // the last step holds one key
+            if (u == 0) tm = tile_max(sS);
+            else if (full) exp_pass<true>(sS, pw, nvalid, sv2, m, &tm, &lt);
+            else exp_pass<false>(sS, pw, nvalid, sv2, m, &tm, &lt);
+            const float mn = fmaxf(m, tm);
+            const bool resc = (__ballot_sync(0xffffffffu, mn > m + thr) & half) != 0;
+            if (__any_sync(0xffffffffu, resc)) {
+                float sc = 1.0f;
+                if (resc) {  // every row of a rescaling slice takes its max
+                    sc = ex2((m - mn) * sinv);
+                    l *= sc;
+                    m = mn;
                 }
-                if ((__ballot_sync(0xffffffffu, tm < m - dthr) & half) == half) {  // dead slice: P zero, l unchanged
-                    zero_prow(prow);
-                    lt = 0.f;
+                if (u > 0) {  // O holds P V of the earlier steps (complete): rescale it in TMEM, factor 1 for the
+                              // slice that keeps its max (TMEM access is warp-collective)
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        float v[16];
+                        tmem_ld16(sO + c * 16, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) v[i] *= sc;
+                        tmem_st16(sO + c * 16, v);
+                    }
+                    tmem_wait_st();
                 }
-                l += lt;
+                // (re)compute P with the refreshed max; the other slice recomputes the same values
+                float tm2;
+                if (full) exp_pass<true>(sS, pw, nvalid, sv2, m, &tm2, &lt);
+                else exp_pass<false>(sS, pw, nvalid, sv2, m, &tm2, &lt);
             }
-            // S_g,u fully read: the tensor core may overwrite it with S_g,u+1
+            if ((__ballot_sync(0xffffffffu, tm < m - dthr) & half) == half) {  // dead slice: P zero, l unchanged
+#pragma unroll
+                for (int i = 0; i < 16; i++) pw[i] = 0;
+                lt = 0.f;
+            }
+            l += lt;
+            // P_g,u (the row's 64 E4M3 values) into the first 16 columns of S_g: the A operand of PV_g,u
+            tmem_st16u(sS, pw);
+            tmem_wait_st();
             tc_fence_before();
-            fence_proxy_async_smem();  // P (generic-proxy stores) -> visible to the tensor core
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&s_free[g]);
-                mbar_arrive(&gp_full[pb]);
-            }
+            if (lane == 0) mbar_arrive(&p_full[g]);
         }
-        if (ok) {
-            const int wl = ATT_NSUB - 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(&gpv_done[wl & 1], (wl >> 1) & 1, err, XTB_ERR_WAIT_ATTN));
-        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[g], (ATT_NSUB - 1) & 1, err, XTB_ERR_WAIT_ATTN));
         if (ok) {
             tc_fence_after();
             const float f = vo / l;
@@ -354,7 +314,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         tmem_dealloc(tbase, 256);
     }
 }
-
 
 // Query row 1024 of every (head, image): one CTA of 256 threads each, in parallel over keys instead of a sequential
 // walk over the 17 key tiles. The walk only matters through the running max, and for a single row it is a scan over
