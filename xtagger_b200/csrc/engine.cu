@@ -3,7 +3,8 @@
 // Bring-up (eva_open / eva_open_ex -> boot thread): read the weight file (v3 per-tensor or v4 block-scaled) into
 // pinned host memory, copy it to every device, resolve the tensor layout, allocate the activations for the
 // device's batch, build the TMA descriptors, capture the whole forward (220 launches) into one CUDA graph per
-// device. Per batch (eva_submit): H2D of the inputs (adjacent pool inputs in one copy), graph launch, D2H of the
+// device (one per input buffer). Per batch (eva_submit): H2D of the inputs (adjacent pool inputs in one copy) on a
+// copy stream into one of two input buffers, graph launch once they have landed, D2H of the
 // scores (and head inputs), event; eva_wait sleeps on the events. Multi-GPU: one replica per device with its own
 // stream and graph; a submit's inputs are split into contiguous shards, one per device, and the scores land in
 // disjoint rows of one host slot. No collective is involved.
@@ -58,9 +59,17 @@ struct Replica {
     Operand op_in, op_pe, op_h, op_h8, op_hw, op_pn;
     Weight8 whead;
     Attn attn;
-    cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t graph = nullptr;   // the forward reading input buffer 0 (in)
     cudaEvent_t done[EVA_NBUF] = {};
     int launches = 0;
+    // submits alternate between two input buffers so that the copies of one batch (on cst) overlap the forward of
+    // the previous one (on st): graph reads in, graph_b reads in_b; in_ready[k] / in_free[k] order the copy stream
+    // and the compute stream for buffer k
+    __half *in_b = nullptr;             // input buffer 1 (buffer 0 is in)
+    cudaGraphExec_t graph_b = nullptr;  // the forward reading in_b
+    cudaStream_t cst = nullptr;
+    cudaEvent_t in_ready[2] = {}, in_free[2] = {};
+    int ib = 0;                         // input buffer of the next submit
 };
 
 struct Impl {
@@ -296,6 +305,7 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     ECK(cudaSetDevice(r.dev));
     RCK(prepare_kernels());
     ECK(cudaStreamCreateWithFlags(&r.st, cudaStreamNonBlocking));
+    ECK(cudaStreamCreateWithFlags(&r.cst, cudaStreamNonBlocking));
     ECK(cudaMalloc(&r.wts, im->wbytes));
     ECK(cudaMemcpyAsync(r.wts, hostblob, im->wbytes, cudaMemcpyHostToDevice, r.st));
     int off = layout(im, r, hostblob);
@@ -328,6 +338,7 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     }
     // activations
     ECK(cudaMalloc(&r.in, (size_t)nb * EVA_IN * 2));
+    ECK(cudaMalloc(&r.in_b, (size_t)nb * EVA_IN * 2));
     ECK(cudaMalloc(&r.x, (size_t)rows * D * 2));
     ECK(cudaMalloc(&r.h, (size_t)rows * D));
     const size_t qkb = (size_t)nb * NH * TP * HD;
@@ -363,18 +374,26 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     RCK(make_attn(&r.attn, r.q8, r.k8, r.v8, nb));
     for (int s = 0; s < EVA_NBUF; s++)
         ECK(cudaEventCreateWithFlags(&r.done[s], cudaEventDisableTiming | cudaEventBlockingSync));
-    ECK(cudaStreamSynchronize(r.st));
-    // capture the forward once
-    cudaGraph_t g;
-    ECK(cudaStreamBeginCapture(r.st, cudaStreamCaptureModeThreadLocal));
-    if (forward(im, r, e, nullptr)) {
-        cudaStreamEndCapture(r.st, &g);
-        return -1;
+    for (int k = 0; k < 2; k++) {
+        ECK(cudaEventCreateWithFlags(&r.in_ready[k], cudaEventDisableTiming));
+        ECK(cudaEventCreateWithFlags(&r.in_free[k], cudaEventDisableTiming));
     }
-    ECK(cudaStreamEndCapture(r.st, &g));
-    ECK(cudaGraphInstantiate(&r.graph, g, 0));
-    ECK(cudaGraphDestroy(g));
-    ECK(cudaGraphUpload(r.graph, r.st));
+    ECK(cudaStreamSynchronize(r.st));
+    // capture the forward once per input buffer
+    for (int k = 0; k < 2; k++) {
+        RCK(make_operand(&r.op_in, k ? r.in_b : r.in, nb * NP, K0P * 2, 128));
+        cudaGraph_t g;
+        ECK(cudaStreamBeginCapture(r.st, cudaStreamCaptureModeThreadLocal));
+        if (forward(im, r, e, nullptr)) {
+            cudaStreamEndCapture(r.st, &g);
+            return -1;
+        }
+        ECK(cudaStreamEndCapture(r.st, &g));
+        ECK(cudaGraphInstantiate(k ? &r.graph_b : &r.graph, g, 0));
+        ECK(cudaGraphDestroy(g));
+        ECK(cudaGraphUpload(k ? r.graph_b : r.graph, r.st));
+    }
+    RCK(make_operand(&r.op_in, r.in, nb * NP, K0P * 2, 128));  // direct (profiling) forwards read buffer 0
     ECK(cudaStreamSynchronize(r.st));
     return 0;
 }
@@ -601,14 +620,23 @@ int eva_submit(eva *e, uint32_t buf, uint16_t *const *in, uint32_t n)
         uint32_t off, cnt;
         shard(im, n, i, &off, &cnt);
         ECK(cudaSetDevice(r.dev));
-        for (uint32_t a = 0, b; a < cnt; a = b) {  // runs of adjacent pool inputs go in one copy
-            for (b = a + 1; b < cnt && in[off + b] == in[off + b - 1] + EVA_IN; b++) {
-            }
-            ECK(cudaMemcpyAsync(r.in + (size_t)a * EVA_IN, in[off + a], (size_t)(b - a) * EVA_IN * 2,
-                                cudaMemcpyHostToDevice, r.st));
-        }
         if (cnt) {
-            ECK(cudaGraphLaunch(r.graph, r.st));
+            // inputs on the copy stream into the buffer the forward before last has finished reading, so they
+            // overlap the previous submit's forward
+            const int k = r.ib;
+            r.ib ^= 1;
+            __half *dst = k ? r.in_b : r.in;
+            ECK(cudaStreamWaitEvent(r.cst, r.in_free[k], 0));
+            for (uint32_t a = 0, b; a < cnt; a = b) {  // runs of adjacent pool inputs go in one copy
+                for (b = a + 1; b < cnt && in[off + b] == in[off + b - 1] + EVA_IN; b++) {
+                }
+                ECK(cudaMemcpyAsync(dst + (size_t)a * EVA_IN, in[off + a], (size_t)(b - a) * EVA_IN * 2,
+                                    cudaMemcpyHostToDevice, r.cst));
+            }
+            ECK(cudaEventRecord(r.in_ready[k], r.cst));
+            ECK(cudaStreamWaitEvent(r.st, r.in_ready[k], 0));
+            ECK(cudaGraphLaunch(k ? r.graph_b : r.graph, r.st));
+            ECK(cudaEventRecord(r.in_free[k], r.st));
             ECK(cudaMemcpyAsync(e->hout[buf] + (size_t)off * e->nt, r.out, (size_t)cnt * e->nt * 4,
                                 cudaMemcpyDeviceToHost, r.st));
             if (e->hpn[buf])
@@ -709,10 +737,16 @@ void eva_close(eva *e)
     for (Replica &r : im->reps) {
         if (cudaSetDevice(r.dev) != cudaSuccess) continue;
         if (r.st) cudaStreamSynchronize(r.st);
+        if (r.cst) cudaStreamSynchronize(r.cst);
         if (r.graph) cudaGraphExecDestroy(r.graph);
+        if (r.graph_b) cudaGraphExecDestroy(r.graph_b);
         for (int s = 0; s < EVA_NBUF; s++)
             if (r.done[s]) cudaEventDestroy(r.done[s]);
-        void *bufs[] = {r.in, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp};
+        for (int k = 0; k < 2; k++) {
+            if (r.in_ready[k]) cudaEventDestroy(r.in_ready[k]);
+            if (r.in_free[k]) cudaEventDestroy(r.in_free[k]);
+        }
+        void *bufs[] = {r.in, r.in_b, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp};
         for (void *p : bufs)
             if (p) cudaFree(p);
         if (r.head_copy) {
@@ -721,6 +755,7 @@ void eva_close(eva *e)
             if (im->head8) cudaFree(r.hws);
         }
         if (r.st) cudaStreamDestroy(r.st);
+        if (r.cst) cudaStreamDestroy(r.cst);
     }
     for (int s = 0; s < EVA_NBUF; s++) {
         if (im->out_reg) {
