@@ -1,5 +1,5 @@
 """The reference's own FP8 flash attention (flash8<1025>, kern_common.cuh:403-543, compiled from the reference's
-header by oracle/Makefile `ref` into oracle/_ref/) run on the GPU next to the oracle's restatement and this
+sources by oracle/Makefile `ref` into oracle/_ref/) run on the GPU next to the oracle's restatement and this
 library's kernel, on the same inputs: it pins the oracle's attention semantics (64-key tiles, lazy rescale and dead
 tiles decided per 16-row warp slice, E4M3 P, fp16-staged output) to the reference's code, and checks this library's
 kernel against the reference directly.
@@ -19,14 +19,14 @@ from tests import _gpu as G
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_SO = os.path.join(ROOT, "oracle", "_ref", "libref_attention.so")
+REF_SO = os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so")
 NIMG, TP, T, D = 2, 1152, 1025, 1024
 
 
 @pytest.fixture(scope="module")
 def ref():
     if not os.path.exists(REF_SO):
-        pytest.skip("oracle/_ref/libref_attention.so not built (python -c 'import __graft_entry__ as g; g.build()' "
+        pytest.skip("oracle/_ref/libref_kernels.so not built (python -c 'import __graft_entry__ as g; g.build()' "
                     "where the reference sources are present)")
     lib = C.CDLL(REF_SO)
     u8 = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
