@@ -291,3 +291,149 @@ extern "C" int ref_forward_time(const char *path, const uint16_t *in, int nimg, 
     release(&B, &m);
     return rc;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Per-kernel entry points (host buffers in this library's layouts; per-tensor multipliers as in v3): the reference's
+// k_ln, k_qkv, k_oproj and k_fc1 + k_fc2, each launched with the grid eva_forward gives it (rows padded to 16 where
+// the reference pads them).
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+template <class E>
+struct Dev {
+    E *p = nullptr;
+    ~Dev()
+    {
+        if (p) cudaFree(p);
+    }
+};
+unsigned pad16(unsigned rows) { return (rows + 15) & ~15u; }
+
+// logical dim of the byte at position s of a q / k row written by k_qkv (eva_kernels.cu:77-79: the dim pair
+// (8 a + 2 c, + 1) lands at 16 (a >> 1) + 4 c + 2 (a & 1))
+int qk_dim(int s) { return 8 * (2 * (s >> 4) + ((s & 3) >> 1)) + 2 * ((s & 15) >> 2) + (s & 1); }
+}  // namespace
+
+// y = E4M3(LN(x) * qs) for rows rows of 1024 fp16 values.
+extern "C" int ref_ln(const uint16_t *x, const float *g, const float *b, int rows, float qs, uint8_t *y)
+{
+    const unsigned M = pad16(rows);
+    Dev<__half> dx;
+    Dev<unsigned char> dy;
+    Dev<float> dg, db;
+    CK(cudaMalloc(&dx.p, (size_t)M * D * 2));
+    CK(cudaMalloc(&dy.p, (size_t)M * D));
+    CK(cudaMalloc(&dg.p, D * 4));
+    CK(cudaMalloc(&db.p, D * 4));
+    CK(cudaMemset(dx.p, 0, (size_t)M * D * 2));
+    CK(cudaMemcpy(dx.p, x, (size_t)rows * D * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dg.p, g, D * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(db.p, b, D * 4, cudaMemcpyHostToDevice));
+    k_ln<<<M >> 3, 256>>>(dx.p, dg.p, db.p, dy.p, M, qs);
+    CK(cudaGetLastError());
+    CK(cudaMemcpy(y, dy.p, (size_t)rows * D, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// q8 / k8 / v8 (this library's layout [nimg][16][tp_out][64], rows >= 1025 left as given) from h (E4M3 [rows][1024],
+// rows = nimg * 1025) and w (E4M3 [3072][1024]); alpha = weight x activation dequantisation.
+extern "C" int ref_qkv(const uint8_t *h, int rows, const uint8_t *w, const float *cs, float alpha, float cq, float ck,
+                       float cv, uint8_t *q8, uint8_t *k8, uint8_t *v8, int tp_out)
+{
+    if (rows % T) return -1;
+    const int nimg = rows / T;
+    const size_t qk = (size_t)nimg * 16 * TP * 64, vt = (size_t)nimg * 16 * NKT * 4096;
+    Dev<unsigned char> dh, dw, dq, dk, dv;
+    Dev<float> dcs;
+    CK(cudaMalloc(&dh.p, (size_t)rows * D));
+    CK(cudaMalloc(&dw.p, (size_t)3 * D * D));
+    CK(cudaMalloc(&dq.p, qk));
+    CK(cudaMalloc(&dk.p, qk));
+    CK(cudaMalloc(&dv.p, vt));
+    CK(cudaMalloc(&dcs.p, (size_t)NP * 64 * 4));
+    CK(cudaMemcpy(dh.p, h, (size_t)rows * D, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dw.p, w, (size_t)3 * D * D, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dcs.p, cs, (size_t)NP * 64 * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemset(dq.p, 0, qk));
+    CK(cudaMemset(dk.p, 0, qk));
+    CK(cudaMemset(dv.p, 0, vt));
+    k_qkv<<<dim3(3 * D / 128, (rows + 127) / 128), 128>>>(dh.p, dw.p, dq.p, dk.p, dv.p, dcs.p, alpha, cq, ck, cv,
+                                                          (unsigned)rows);
+    CK(cudaGetLastError());
+    std::vector<unsigned char> q(qk), k(qk), v(vt);
+    CK(cudaMemcpy(q.data(), dq.p, qk, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(k.data(), dk.p, qk, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(v.data(), dv.p, vt, cudaMemcpyDeviceToHost));
+    for (size_t bh = 0; bh < (size_t)nimg * 16; bh++)
+        for (int t = 0; t < T; t++)
+            for (int s = 0; s < 64; s++) {
+                q8[(bh * tp_out + t) * 64 + qk_dim(s)] = q[(bh * TP + t) * 64 + s];
+                k8[(bh * tp_out + t) * 64 + qk_dim(s)] = k[(bh * TP + t) * 64 + s];
+                v8[(bh * tp_out + t) * 64 + s] = v[(bh * NKT + (t >> 6)) * 4096 + s * 64 + (t & 63)];
+            }
+    return 0;
+}
+
+// x (fp16 [rows][1024], in / out) += alpha * a w^T, a E4M3 [rows][1024], w E4M3 [1024][1024].
+extern "C" int ref_oproj(const uint8_t *a, int rows, const uint8_t *w, float alpha, uint16_t *x)
+{
+    Dev<unsigned char> da, dw;
+    Dev<__half> dx;
+    CK(cudaMalloc(&da.p, (size_t)rows * D));
+    CK(cudaMalloc(&dw.p, (size_t)D * D));
+    CK(cudaMalloc(&dx.p, (size_t)rows * D * 2));
+    CK(cudaMemcpy(da.p, a, (size_t)rows * D, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dw.p, w, (size_t)D * D, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dx.p, x, (size_t)rows * D * 2, cudaMemcpyHostToDevice));
+    k_oproj<<<dim3(D / 128, (rows + 127) / 128), 128>>>(da.p, dw.p, dx.p, alpha, (unsigned)rows);
+    CK(cudaGetLastError());
+    CK(cudaMemcpy(x, dx.p, (size_t)rows * D * 2, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// The MLP: k_fc1 (h8 = E4M3(rs * SwiGLU(a12 * h W12^T)), per-tile row statistics) then k_fc2 (x += rstd * (a3 * h8
+// W2^T - mean * cn) + dn). Outputs h8 [rows][2736], the row totals of the statistics (sum u, sum u^2, summed over the
+// reference's 57 partials in double), and x (in / out).
+extern "C" int ref_mlp(const uint8_t *h, int rows, const uint8_t *w12, const float *rs, float a12, const uint8_t *w2,
+                       const float *cn, const float *dn, float a3, uint8_t *h8, double *rowsum, double *rowsq, uint16_t *x)
+{
+    const unsigned M = pad16(rows);
+    Dev<unsigned char> dh, dw12, dw2, dh8;
+    Dev<float> drs, dst, dcn, ddn;
+    Dev<__half> dx;
+    CK(cudaMalloc(&dh.p, (size_t)M * D));
+    CK(cudaMalloc(&dw12.p, (size_t)2 * HIDP * D));
+    CK(cudaMalloc(&dw2.p, (size_t)D * HIDP));
+    CK(cudaMalloc(&dh8.p, (size_t)M * HIDP));
+    CK(cudaMalloc(&drs.p, HIDP * 4));
+    CK(cudaMalloc(&dst.p, (size_t)NCT * M * 2 * 4));
+    CK(cudaMalloc(&dcn.p, D * 4));
+    CK(cudaMalloc(&ddn.p, D * 4));
+    CK(cudaMalloc(&dx.p, (size_t)M * D * 2));
+    CK(cudaMemset(dh.p, 0, (size_t)M * D));
+    CK(cudaMemset(dx.p, 0, (size_t)M * D * 2));
+    CK(cudaMemcpy(dh.p, h, (size_t)rows * D, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dw12.p, w12, (size_t)2 * HIDP * D, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dw2.p, w2, (size_t)D * HIDP, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(drs.p, rs, HIDP * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dcn.p, cn, D * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ddn.p, dn, D * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dx.p, x, (size_t)rows * D * 2, cudaMemcpyHostToDevice));
+    k_fc1<<<dim3((M + 127) / 128, NCT), 128>>>(dh.p, dw12.p, dh8.p, dst.p, drs.p, a12, M);
+    CK(cudaGetLastError());
+    k_fc2<<<dim3(D / 128, (M + 127) / 128), 128>>>(dh8.p, dw2.p, dx.p, dst.p, dcn.p, ddn.p, a3, M);
+    CK(cudaGetLastError());
+    std::vector<float> st((size_t)NCT * M * 2);
+    CK(cudaMemcpy(h8, dh8.p, (size_t)rows * HIDP, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(st.data(), dst.p, st.size() * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(x, dx.p, (size_t)rows * D * 2, cudaMemcpyDeviceToHost));
+    for (int r = 0; r < rows; r++) {
+        double s = 0, q = 0;
+        for (int c = 0; c < NCT; c++) {
+            s += st[((size_t)c * M + r) * 2];
+            q += st[((size_t)c * M + r) * 2 + 1];
+        }
+        rowsum[r] = s;
+        rowsq[r] = q;
+    }
+    return 0;
+}
