@@ -133,7 +133,7 @@ def run_reference(args, rank, world):
     line = {"metric": METRIC, "value": v, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config 3 (EVA02-L 448^2 forward, 24 layers, 10861 tags); each step a bounded "
+            "config": {"workload": f"{config_name(args)} (EVA02-L 448^2 forward, 24 layers, {args.nt} tags); each step a bounded "
                                    "sample of 1 image on the host cores", "global_batch": args.batch},
             "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": "port",
                              "sample": "1 image per step, full 24-layer forward, CPU restatement (oracle/) of the "
@@ -229,13 +229,13 @@ def run_ours(args, rank, world, local):
         line = {"metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
-                "config": {"workload": "config 3: EVA02-L 448^2 forward (24 layers, d 1024, 1025 tokens, 10861-tag "
+                "config": {"workload": f"{config_name(args)}: EVA02-L 448^2 forward (24 layers, d 1024, 1025 tokens, {args.nt}-tag "
                                        "FP8 head), global batch split across the GPUs",
                            "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
                            "weights": "random-init, E4M3 with fp32 scales per 128x128 block",
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
                 "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": args.batch * 1024 * 592 * 2,
-                        "d2h_bytes_per_step": args.batch * NT * 4},
+                        "d2h_bytes_per_step": args.batch * args.nt * 4},
                 "roofline": {"bound": "tensor", "kernel": "fc1 (tcgen05 E4M3 GEMM + SwiGLU epilogue)",
                              "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                              "peak_source": peak_src, "flop_per_launch": FC1_FLOP_PER_ROW * rows,
@@ -252,6 +252,17 @@ def run_ours(args, rank, world, local):
         pg.destroy_process_group()
 
 
+def config_name(args):
+    """The benchmark-plan config a run corresponds to (2: batch 1; 3: batch 64; 4: batch 32 with 13461 tags)."""
+    if args.nt == NT and args.batch == 1:
+        return "config 2"
+    if args.nt == NT and args.batch == 64:
+        return "config 3"
+    if args.nt == 13461 and args.batch == 32:
+        return "config 4"
+    return f"batch {args.batch}, {args.nt} tags"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -260,8 +271,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
     args = ap.parse_args()
     rank, world, local = dist_env()
+    MODEL_KW["nt"] = args.nt
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -25,13 +25,15 @@ def main():
     ap.add_argument("--batch", type=int, nargs="+", default=[8, 64])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--nt", type=int, default=10861)
     a = ap.parse_args()
     from xtagger_b200 import model as M
     lib = C.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so"))
     lib.ref_forward_time.restype = C.c_int
     lib.ref_forward_time.argtypes = [C.c_char_p, np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS"), C.c_int,
                                      C.c_int, C.c_int, C.POINTER(C.c_float)]
-    path = M.write_synthetic(os.path.join(tempfile.mkdtemp(), "v3.bin"), seed=0, nl=24, version=3, head_fp8=False)
+    path = M.write_synthetic(os.path.join(tempfile.mkdtemp(), "v3.bin"), seed=0, nt=a.nt, nl=24, version=3,
+                             head_fp8=False)
     for nb in a.batch:
         x = np.ascontiguousarray(M.synthetic_inputs(nb, seed=1))
         ms = C.c_float(0)
@@ -39,7 +41,7 @@ def main():
             raise SystemExit("reference forward failed")
         print(json.dumps({"impl": "reference kernels (eva_kernels.cu, mma.sync E4M3) on this GPU", "batch": nb,
                           "ms_per_forward": ms.value, "images_per_s": nb / (ms.value * 1e-3),
-                          "model": "v3, 24 layers, fp16 head, 10861 tags, random-init"}), flush=True)
+                          "model": f"v3, 24 layers, fp16 head, {a.nt} tags, random-init"}), flush=True)
 
 
 if __name__ == "__main__":
