@@ -151,6 +151,31 @@ int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *p
 int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x,
                     const float *stat, const float *c, const float *d, void *stream);
 
+/* ---- 2:4-sparse weights on the sparse tensor cores (tcgen05.mma.sp) ----
+ * The reference prunes weights 2:4 offline (prune24.py:44-56: in every group of four consecutive k the two least
+ * important bytes are zeroed) and runs them through its dense kernels. These entry points run such weights on the
+ * sparse MMA instead, with the same results as the dense xtb_qkv / xtb_oproj / xtb_fc1 / xtb_fc2 on the same
+ * weights (same epilogue arithmetic; only the order of the fp32 sums inside a 128-k block may differ).
+ * Compressed form (host memory, from xtb_sparse24_compress): values [np][kp / 2] (the two kept bytes of every group
+ * of four, in k order) and metadata [np][kp / 8] (per group the in-group indices i0 < i1 of the kept bytes as
+ * i0 | i1 << 2, two groups per byte, low nibble first), np / kp = n / k rounded up to a multiple of 128. */
+/* 1 if every group of four consecutive k of every row of w [n][k] holds at most two nonzero E4M3 codes. */
+int xtb_sparse24_check(const uint8_t *w, int n, int k);
+/* Compress a 2:4 weight (host pointers; vals np * kp / 2 bytes, meta np * kp / 8 bytes). 0, or -1 if not 2:4. */
+int xtb_sparse24_compress(const uint8_t *w, int n, int k, uint8_t *vals, uint8_t *meta);
+/* out[m][n] (fp32) = ascale * sum_k x[m][k] W[n][k] * wscale[n / 128][k / 128], W compressed (device pointers). */
+int xtb_gemm_sp_e4m3_f32(const uint8_t *x, int m, int k, const uint8_t *vals, const uint8_t *meta, int n,
+                         const float *wscale, float ascale, float *out, void *stream);
+/* As xtb_qkv / xtb_oproj / xtb_fc1 / xtb_fc2 with the weight compressed (vals, meta) and its block scales ws. */
+int xtb_qkv_sp(const uint8_t *h, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+               uint8_t *q8, uint8_t *k8, uint8_t *v8, const float *cs, float cq, float ck, float cv, void *stream);
+int xtb_oproj_sp(const uint8_t *a, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+                 uint16_t *x, void *stream);
+int xtb_fc1_sp(const uint8_t *h, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+               uint8_t *h8, float *stat, const float *rs, void *stream);
+int xtb_fc2_sp(const uint8_t *h8, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+               uint16_t *x, float *stat, const float *c, const float *d, void *stream);
+
 /* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). */
 uint32_t xtb_error_word(int device);
 void xtb_error_clear(int device);

@@ -130,6 +130,74 @@ int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *p
     return launch_head_e4m3(W, B, ascale, nimg, nt, hb, out, S(stream));
 }
 
+// ---- 2:4-sparse weights ----
+int xtb_sparse24_check(const uint8_t *w, int n, int k) { return sparse24_check(w, n, k); }
+
+int xtb_sparse24_compress(const uint8_t *w, int n, int k, uint8_t *vals, uint8_t *meta)
+{
+    if (!vals || !meta) return -1;
+    return sparse24_compress(w, n, k, vals, meta);
+}
+
+static int sp_weight(SparseW *w, const uint8_t *vals, const uint8_t *meta, int n, int k, const float *ws)
+{
+    return make_sparse_weight(w, vals, meta, n, k, ws);
+}
+
+int xtb_gemm_sp_e4m3_f32(const uint8_t *x, int m, int k, const uint8_t *vals, const uint8_t *meta, int n,
+                         const float *wscale, float ascale, float *out, void *stream)
+{
+    Operand X;
+    SparseW W;
+    if (m <= 0 || n <= 0 || k <= 0 || (k & 15)) {
+        fprintf(stderr, "eva: xtb_gemm_sp_e4m3_f32: bad shape m %d n %d k %d (k must be a multiple of 16)\n", m, n, k);
+        return -1;
+    }
+    if (make_operand(&X, x, m, k, SP_BOX_ROWS) || sp_weight(&W, vals, meta, n, k, wscale)) return -1;
+    return launch_gemm_sp_f32(X, W, ascale, out, n, S(stream));
+}
+
+int xtb_qkv_sp(const uint8_t *h, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+               uint8_t *q8, uint8_t *k8, uint8_t *v8, const float *cs, float cq, float ck, float cv, void *stream)
+{
+    Operand A;
+    SparseW W;
+    if (!rows_ok(rows, "xtb_qkv_sp") || make_operand(&A, h, rows, D, SP_BOX_ROWS) || sp_weight(&W, vals, meta, 3 * D, D, ws))
+        return -1;
+    return launch_qkv_sp(A, W, ascale, rows, q8, k8, v8, cs, cq, ck, cv, S(stream));
+}
+
+int xtb_oproj_sp(const uint8_t *a, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+                 uint16_t *x, void *stream)
+{
+    Operand A;
+    SparseW W;
+    if (!rows_ok(rows, "xtb_oproj_sp") || make_operand(&A, a, rows, D, SP_BOX_ROWS) || sp_weight(&W, vals, meta, D, D, ws))
+        return -1;
+    return launch_oproj_sp(A, W, ascale, rows, (__half *)x, S(stream));
+}
+
+int xtb_fc1_sp(const uint8_t *h, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+               uint8_t *h8, float *stat, const float *rs, void *stream)
+{
+    Operand A;
+    SparseW W;
+    if (!rows_ok(rows, "xtb_fc1_sp") || make_operand(&A, h, rows, D, SP_BOX_ROWS) || sp_weight(&W, vals, meta, N12, D, ws))
+        return -1;
+    return launch_fc1_sp(A, W, ascale, rows, h8, (float2 *)stat, rs, S(stream));
+}
+
+int xtb_fc2_sp(const uint8_t *h8, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
+               uint16_t *x, float *stat, const float *c, const float *d, void *stream)
+{
+    Operand A;
+    SparseW W;
+    if (!rows_ok(rows, "xtb_fc2_sp") || make_operand(&A, h8, rows, HIDP, SP_BOX_ROWS) ||
+        sp_weight(&W, vals, meta, D, HIDP, ws))
+        return -1;
+    return launch_fc2_sp(A, W, ascale, rows, (__half *)x, (float2 *)stat, c, d, S(stream));
+}
+
 uint32_t xtb_error_word(int device)
 {
     uint32_t *p = error_word(device), v = 0;

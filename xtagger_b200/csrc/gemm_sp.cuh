@@ -1,0 +1,448 @@
+// 2:4-sparse block-scaled FP8 GEMM on tcgen05.mma.sp (sm_100a), the weights as the sparse operand:
+//     D[n][t] = epilogue( sum_k W[n][k] * X[t][k] )        n: weight row (output feature), t: token
+// tcgen05 takes sparsity on the A operand only, so the weights are A (128 rows per tile, one per TMEM lane) and the
+// activations are B (SP_BT = 224 tokens per tile, TMEM columns): the accumulator holds the transposed output. The
+// epilogues below are the transposed forms of those in epilogues.cuh, with the same arithmetic per (token,
+// feature), so that on pruned weights this path reproduces the dense one (the reference runs pruned weights,
+// prune24.py's output, through its dense kernels: this is the same product on the sparse tensor-core path).
+//
+// Weight format (sparse24_compress, sparse24.cu): values [Np][Kp / 2] = the two kept bytes of every group of four
+// consecutive k, in k order; metadata [Np][Kp / 8] = per group the in-group index of the first kept byte in bits
+// 0-1 and of the second in bits 2-3 (first < second), groups in k order, two per byte, low nibble first. Np and Kp
+// are padded to multiples of 128 (padding groups: zero values, indices 0 and 1). This is the layout
+// tcgen05.mma.sp reads for kind::f8f6f4 at M = 128: metadata row n in TMEM lane n, 16 bytes (4 columns) per
+// 128 k, 2 columns per K = 64 instruction.
+//
+// Pipeline stage = one 128-element K block (one block scale): 128 weight rows x 64 value bytes (64B swizzle),
+// 128 x 16 metadata bytes (unswizzled), 224 tokens x 128 activation bytes (128B swizzle).
+// Warps (320 threads): 0 TMA producer; 1 TMEM allocation and MMA issue (tcgen05.cp of the stage's metadata into
+// TMEM, then two K = 64 sparse MMAs); 2..9 epilogue: warp w reads TMEM lanes 32 (w % 4) .. (32 features) and the
+// token half (w - 2) / 4 of the tile (112 columns), promoting the block scales per K block as gemm.cuh does.
+// TMEM: accumulators at columns [0, 224) and [224, 448) (ping-pong per K block), metadata at 448 and 452
+// (ping-pong per K block; a metadata column must be even).
+#pragma once
+#include "gemm.cuh"
+#include "ops.h"
+
+namespace xtb {
+
+constexpr int SP_BT = 224;          // tokens per tile (MMA N)
+constexpr int SP_COLS = SP_BT / 2;  // token columns per epilogue thread
+
+struct SpCfg {
+    static constexpr int A_BYTES = 128 * 64;
+    static constexpr int E_BYTES = 128 * 16;
+    static constexpr int B_BYTES = SP_BT * 128;
+    static constexpr int STAGE_BYTES = A_BYTES + E_BYTES + B_BYTES;
+    static constexpr int STAGES = 4;
+    static constexpr int EW = 8;
+    static constexpr int STAGE_PER_WARP = SP_COLS * 64;      // 112 tokens x 32 fp16 features
+    static constexpr int XRED_FLOAT2 = 2 * 2 * 4 * SP_COLS;  // fc1 statistics exchange [half][buffer][quad][token]
+    static constexpr int E_COL = 2 * SP_BT;                  // metadata TMEM columns (two buffers of 4)
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + EW * STAGE_PER_WARP + XRED_FLOAT2 * 8 + 256;
+    static constexpr int THREADS = 64 + 32 * EW;
+    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(E_COL + 8 <= 512, "TMEM budget");
+    static_assert(SP_COLS % 16 == 0, "epilogue drains 16 columns at a time");
+};
+
+struct SpArgs {
+    int M;            // tokens
+    int kiters;       // 128-element K blocks
+    int n_tiles, t_tiles;
+    const float *ws;  // block scales [ws_rows][ws_ld] (row = 128-row weight block)
+    int ws_ld, ws_rows;
+    float ascale;     // activation dequant scale
+    uint32_t *err;
+};
+
+// Epilogue context of one thread: weight row (feature) f0 + lane, tokens t0 .. t0 + SP_COLS - 1.
+struct SpCtx {
+    int f0, t0, nb, lane, quad;
+    uint8_t *stage;            // this warp's staging buffer (STAGE_PER_WARP bytes)
+    float2 *xred;              // this token half's exchange buffers [2][4][SP_COLS]
+    uint64_t *xbar;            // their barriers [2] (one arrival per warp of the half)
+    uint32_t xuse;             // exchanges done by this warp
+    const CUtensorMap *tmC;
+    uint32_t *err;
+};
+
+template <class Epi>
+__global__ void __launch_bounds__(SpCfg::THREADS, 1)
+    k_gemm_sp(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmE,
+              const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC, const SpArgs g,
+              const typename Epi::Params ep)
+{
+    using C = SpCfg;
+    constexpr int STAGES = C::STAGES;
+    constexpr uint32_t IDESC = idesc_sp_m128(SP_BT);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;                       // weight values: 64B-swizzle atoms (512 bytes) need 512-byte alignment
+    uint8_t *sB = sA + STAGES * C::A_BYTES;   // activations: 128B swizzle, 1024-byte aligned (28 KB per stage)
+    uint8_t *sE = sB + STAGES * C::B_BYTES;   // metadata
+    uint8_t *sStage = sE + STAGES * C::E_BYTES;
+    float2 *xred = (float2 *)(sStage + C::EW * C::STAGE_PER_WARP);
+    uint64_t *full = (uint64_t *)(xred + C::XRED_FLOAT2);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *xbar = tempty + 2;              // [half][buffer]
+    uint32_t *tslot = (uint32_t *)(xbar + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], C::EW);
+        }
+        for (int b = 0; b < 4; b++) mbar_init(&xbar[b], 4);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmE);
+        tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmC);
+    }
+    if (warp == 1) {
+        tmem_alloc(tslot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    const int total = g.n_tiles * g.t_tiles;
+    const int KI = g.kiters;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                // weight tiles fastest: the CTAs working at one time share a few token tiles (read from DRAM once,
+                // then from L2), and every layer's weights fit in L2
+                const int nb = t % g.n_tiles, tt = t / g.n_tiles;
+                for (int k = 0; k < KI; k++) {
+                    if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], k * 64, nb * 128);
+                    tma_load_2d(sE + stage * C::E_BYTES, &tmE, &full[stage], k * 16, nb * 128);
+                    tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], k * 128, tt * SP_BT);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {
+            int stage = 0;
+            uint32_t ph = 0, tb = 0, tph = 0, eb = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int k = 0; k < KI; k++) {
+                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
+                    tc_fence_after();
+                    if (!(ok = mbar_wait(&full[stage], ph, g.err, XTB_ERR_WAIT_TMA))) break;
+                    tc_fence_after();
+                    const uint32_t ecol = tbase + C::E_COL + 4 * eb;
+                    tmem_cp_128x128b(ecol, sdesc_rows16(smem_u32(sE + stage * C::E_BYTES)));
+                    const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+                    const uint32_t d = tbase + tb * SP_BT;
+#pragma unroll
+                    for (int kk = 0; kk < 2; kk++)
+                        umma_sp(d, sdesc(a0 + kk * 32, 512, SWZ_64B), sdesc(b0 + kk * 64, 1024, SWZ_128B), ecol + 2 * kk,
+                                IDESC, kk > 0);
+                    umma_commit(&empty[stage]);
+                    umma_commit(&tfull[tb]);
+                    eb ^= 1;
+                    if ((tb ^= 1) == 0) tph ^= 1;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+        }
+    } else {
+        const int ew = warp - 2;
+        const int quad = warp & 3;
+        const int half = ew >> 2;  // which 112-token half of the tile
+        SpCtx cx;
+        cx.lane = lane;
+        cx.quad = quad;
+        cx.stage = sStage + ew * C::STAGE_PER_WARP;
+        cx.xred = xred + half * (2 * 4 * SP_COLS);
+        cx.xbar = xbar + 2 * half;
+        cx.xuse = 0;
+        cx.tmC = &tmC;
+        cx.err = g.err;
+        uint32_t tb = 0, tph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            const int nb = t % g.n_tiles, tt = t / g.n_tiles;
+            cx.nb = nb;
+            cx.f0 = nb * 128 + quad * 32;
+            cx.t0 = tt * SP_BT + half * SP_COLS;
+            float2 acc[SP_COLS / 2];
+#pragma unroll
+            for (int j = 0; j < SP_COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);
+            const float *wsr = g.ws + (size_t)min(nb, g.ws_rows - 1) * g.ws_ld;
+            float snext = __ldg(wsr);
+            const float amul = g.ascale * Epi::row_scale(ep, cx.f0);
+            for (int u = 0; u < KI; u++) {
+                const float s = amul * snext;
+                if (u + 1 < KI) snext = __ldg(wsr + u + 1);
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
+                tc_fence_after();
+                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * SP_BT + half * SP_COLS;
+                const float2 s2 = make_float2(s, s);
+#pragma unroll
+                for (int c = 0; c < SP_COLS / 16; c++) {
+                    float v[16];
+                    tmem_ld16(taddr + c * 16, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[c * 8 + j] = ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[c * 8 + j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[tb]);
+                if ((tb ^= 1) == 0) tph ^= 1;
+            }
+            if (!ok) break;
+            ok = Epi::apply(ep, (const float *)acc, cx);
+        }
+        if (lane == 0) bulk_wait0();  // the epilogue's TMA stores / reductions have completed
+        __syncwarp();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Transposed epilogues: apply(params, acc[SP_COLS], ctx); acc[j] = output (token ctx.t0 + j, feature ctx.f0 + lane),
+// already dequantised. Tokens past M and features past the problem are skipped. Return false only when a bounded
+// wait ran out.
+// ---------------------------------------------------------------------------------------------------------------
+
+// Plain fp32 store out[t][f] (row stride ld floats): the stand-alone sparse GEMM.
+struct SpF32 {
+    struct Params {
+        float *out;
+        int ld, M, N;
+    };
+    __device__ __forceinline__ static float row_scale(const Params &, int) { return 1.0f; }
+    __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
+    {
+        const int f = cx.f0 + cx.lane;
+        if (f < p.N) {
+#pragma unroll
+            for (int j = 0; j < SP_COLS; j++)
+                if (cx.t0 + j < p.M) p.out[(size_t)(cx.t0 + j) * p.ld + f] = acc[j];
+        }
+        return true;
+    }
+};
+
+// QKV (k_qkv, eva_kernels.cu:41-114), as EpiQKV: q / k rows get the interleaved RoPE of patch tokens (dims 2j and
+// 2j + 1 are neighbouring lanes), v rows are only scaled (cq / ck / cv ride on the block-scale promotion); E4M3 into
+// q8 / k8 / v8 [img][head][TP][64]. A warp holds half a head (32 dims) for 112 tokens: bytes are staged as
+// [token][32] and leave as 16-byte pieces.
+struct SpQKV {
+    struct Params {
+        uint8_t *q8, *k8, *v8;
+        const float2 *cs;
+        float cq, ck, cv;
+        int M;
+    };
+    __device__ __forceinline__ static float row_scale(const Params &p, int f0)
+    {
+        const int which = f0 >> 10;
+        return which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
+    }
+    __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
+    {
+        const int which = cx.f0 >> 10, head = (cx.f0 & 1023) >> 6, dbase = cx.f0 & 63;
+        const int jp = (dbase + cx.lane) >> 1;  // RoPE pair of this lane's dim
+        const bool odd = cx.lane & 1;
+        int tt = cx.t0 % T;
+        __syncwarp();  // the previous tile's copies out of the staging buffer are done
+#pragma unroll
+        for (int j = 0; j < SP_COLS; j++) {
+            float v = acc[j];
+            if (which < 2) {
+                // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin); cls rows and rows past M: cos 1, sin 0
+                const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
+                float2 c = make_float2(1.f, 0.f);
+                if (tt > 0 && cx.t0 + j < p.M) c = __ldg(p.cs + (size_t)(tt - 1) * 32 + jp);
+                v = fmaf(pv, odd ? c.y : -c.y, v * c.x);
+            }
+            cx.stage[j * 32 + cx.lane] = (uint8_t)e4m3x2(v, 0.f);
+            if (++tt == T) tt = 0;
+        }
+        __syncwarp();
+        uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
+#pragma unroll
+        for (int i = 0; i < SP_COLS * 2 / 32; i++) {
+            const int pc = i * 32 + cx.lane;  // piece: token r, 16-byte half ch of its 32 dims
+            const int r = pc >> 1, ch = pc & 1;
+            const int t = cx.t0 + r;
+            if (t < p.M) {
+                const int b = t / T, tq = t - b * T;
+                *(uint4 *)(dst + (((size_t)(b * NH + head) * TP + tq) << 6) + dbase + 16 * ch) =
+                    *(const uint4 *)(cx.stage + r * 32 + 16 * ch);
+            }
+        }
+        return true;
+    }
+};
+
+// fp16 residual update x[t][f] += delta by TMA reduce-add of the warp's 112 tokens x 32 features (the tensor map
+// has boxes of 32 halves x 112 rows, unswizzled): the out-projection (EpiResid, LN = false) and fc2 with the MLP
+// LayerNorm folded in (EpiFC2, LN = true: delta = rstd * (acc - mean * c[f]) + d[f] with (mean, rstd) of the token
+// from k_rowstat).
+template <bool LN>
+struct SpResid {
+    struct Params {
+        const float2 *ms;
+        const float *c, *d;
+        int M;
+    };
+    __device__ __forceinline__ static float row_scale(const Params &, int) { return 1.0f; }
+    __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
+    {
+        if (cx.lane == 0) bulk_wait_read0();  // the previous tile's reduction has read the staging buffer
+        __syncwarp();
+        float cf = 0.f, df = 0.f;
+        if (LN) {
+            cf = __ldg(p.c + cx.f0 + cx.lane);
+            df = __ldg(p.d + cx.f0 + cx.lane);
+        }
+        __half *srow = (__half *)cx.stage + cx.lane;
+#pragma unroll
+        for (int j = 0; j < SP_COLS; j++) {
+            float v = acc[j];
+            if (LN) {
+                const float2 ms = __ldg(p.ms + min(cx.t0 + j, p.M - 1));
+                v = fmaf(ms.y, v, fmaf(-ms.x * ms.y, cf, df));
+            }
+            srow[j * 32] = __float2half_rn(v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (cx.lane == 0 && cx.t0 < p.M) {
+            tma_reduce_add_2d(cx.tmC, cx.stage, cx.f0, cx.t0);
+            bulk_commit();
+        }
+        return true;
+    }
+};
+
+// Sum of v[8] (8 tokens) over the 16 lanes of each half-warp, in a fixed order: on return v[0] of lane l holds the
+// total of token (l >> 1) & 7 (lanes l and l ^ 1 hold the same).
+__device__ __forceinline__ void halfwarp_sum8(float (&v)[8], int lane)
+{
+    const bool b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float send = b3 ? v[i] : v[i + 4];
+        const float keep = b3 ? v[i + 4] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float send = b2 ? v[i] : v[i + 2];
+        const float keep = b2 ? v[i + 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    {
+        const float send = b1 ? v[0] : v[1];
+        const float keep = b1 ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// fc1 + SwiGLU (k_fc1, eva_kernels.cu:211-279), as EpiFC1. The W12 rows interleave g and x in 16-unit chunks, so a
+// warp's lanes 0-15 hold g and lanes 16-31 x of the same 16 units: one exchange gives lanes 0-15 tokens 0..55 and
+// lanes 16-31 tokens 56..111 of (g, x). u = x g sigmoid(g), h8 = E4M3(u rs[unit]) stored by TMA (boxes of 16 units x
+// 112 tokens); the row statistics partial stat[nb][t] (sum u, sum u^2 over the tile's 64 units) is summed across
+// the 16 lanes, then across the four warps of the token half through shared memory.
+struct SpFC1 {
+    struct Params {
+        float2 *stat;
+        const float *rs;
+        int M;
+    };
+    __device__ __forceinline__ static float row_scale(const Params &, int) { return 1.0f; }
+    __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
+    {
+        constexpr int H = SP_COLS / 2;  // tokens per lane after the exchange
+        const int lane = cx.lane;
+        const bool hi = lane >= 16;
+        const int unit = (cx.f0 >> 1) + (lane & 15);
+        const bool live = cx.f0 < N12;  // warp-uniform: false for the padding rows of the last weight tile
+        const float r = (live && unit < HIDP) ? __ldg(p.rs + unit) : 0.0f;
+        const uint32_t buf = cx.xuse & 1;
+        float2 *xr = cx.xred + buf * 4 * SP_COLS;
+        if (lane == 0) bulk_wait_read0();  // the previous tile's h8 store has read the staging buffer
+        __syncwarp();
+        uint8_t *srow = cx.stage + (hi ? H : 0) * 16 + (lane & 15);
+#pragma unroll
+        for (int c = 0; c < H / 8; c++) {
+            float s[8], q[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int j = 8 * c + i;
+                const float send = hi ? acc[j] : acc[H + j];
+                const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+                const float gv = hi ? recv : acc[j];
+                const float xv = hi ? acc[H + j] : recv;
+                const float hg = 0.5f * gv;  // u = x (g/2) (1 + tanh(g/2))
+                const float u = xv * fmaf(hg, tanh_fast(hg), hg);
+                srow[j * 16] = (uint8_t)e4m3x2(u * r, 0.f);
+                s[i] = u;
+                q[i] = u * u;
+            }
+            halfwarp_sum8(s, lane);
+            halfwarp_sum8(q, lane);
+            if (!(lane & 1)) xr[cx.quad * SP_COLS + (hi ? H : 0) + 8 * c + ((lane >> 1) & 7)] = make_float2(s[0], q[0]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && live && cx.t0 < p.M) {
+            tma_store_2d(cx.tmC, cx.stage, cx.f0 >> 1, cx.t0);
+            bulk_commit();
+        }
+        if (lane == 0) mbar_arrive(&cx.xbar[buf]);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(&cx.xbar[buf], (cx.xuse >> 1) & 1, cx.err, XTB_ERR_WAIT_TMEM));
+        if (ok && lane < SP_COLS / 4) {
+            const int tk = (SP_COLS / 4) * cx.quad + lane;
+            float2 a = xr[tk];
+#pragma unroll
+            for (int w = 1; w < 4; w++) {
+                const float2 b = xr[w * SP_COLS + tk];
+                a.x += b.x;
+                a.y += b.y;
+            }
+            const int t = cx.t0 + tk;
+            if (t < p.M) p.stat[(size_t)cx.nb * p.M + t] = a;
+        }
+        cx.xuse++;
+        return ok;
+    }
+};
+
+}  // namespace xtb

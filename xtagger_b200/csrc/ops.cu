@@ -5,6 +5,7 @@
 #include "attention.cuh"
 #include "epilogues.cuh"
 #include "gemm.cuh"
+#include "gemm_sp.cuh"
 #include "host.h"
 #include "ops.h"
 #include "rowops.cuh"
@@ -231,6 +232,106 @@ int launch_fc2_gemm(const Operand &h8, const Weight8 &w, float ascale, int rows,
     return run_proj<EpiFC2, W_FC2>(h8, w, rows, ascale, p, st, &xm, err);
 }
 
+// ---- 2:4-sparse projections ----
+static_assert(SP_BT == SP_BOX_ROWS, "activation box height of the sparse kernels");
+
+int make_sparse_weight(SparseW *w, const uint8_t *vals, const uint8_t *meta, int n, int k, const float *ws)
+{
+    if (n <= 0 || k <= 0 || (k & 3) || !vals || !meta || !ws) {
+        fprintf(stderr, "eva: sparse weight [%d][%d]: bad shape or null pointer\n", n, k);
+        return -1;
+    }
+    w->n = n;
+    w->k = k;
+    w->np = (n + 127) & ~127;
+    w->kp = (k + 127) & ~127;
+    w->ws = ws;
+    if (make_tmap_2d(&w->va, vals, (uint64_t)w->kp / 2, (uint64_t)w->np, (uint64_t)w->kp / 2, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_64B))
+        return -1;
+    return make_tmap_2d(&w->me, meta, (uint64_t)w->kp / 8, (uint64_t)w->np, (uint64_t)w->kp / 8, 16, 128,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// One launch of the sparse GEMM: persistent grid of one CTA per SM over (weight tile, token tile) pairs.
+template <class Epi>
+static int run_gemm_sp(const SparseW &w, const Operand &x, int M, float ascale, const typename Epi::Params &ep,
+                       cudaStream_t st, const CUtensorMap *tmc = nullptr)
+{
+    auto kern = k_gemm_sp<Epi>;
+    if (set_smem((const void *)kern, SpCfg::SMEM)) return -1;
+    if (x.row_bytes != w.k || x.box_rows != SP_BOX_ROWS || M <= 0 || M > x.rows) {
+        fprintf(stderr, "eva: sparse gemm operands (K bytes %d vs %d, box %d rows, M %d of %d)\n", x.row_bytes, w.k,
+                x.box_rows, M, x.rows);
+        return -1;
+    }
+    const int dev = current_device();
+    SpArgs g;
+    g.M = M;
+    g.kiters = w.kp / 128;
+    g.n_tiles = w.np / 128;
+    g.t_tiles = (M + SP_BT - 1) / SP_BT;
+    g.ws = w.ws;
+    g.ws_ld = kb(w.k);
+    g.ws_rows = kb(w.n);
+    g.ascale = ascale;
+    g.err = error_word(dev);
+    const int total = g.n_tiles * g.t_tiles;
+    int grid = num_sms(dev);
+    if (grid > total) grid = total;
+    kern<<<grid, SpCfg::THREADS, SpCfg::SMEM, st>>>(w.va, w.me, x.map, tmc ? *tmc : x.map, g, ep);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
+int launch_gemm_sp_f32(const Operand &x, const SparseW &w, float ascale, float *out, int ldo, cudaStream_t st)
+{
+    SpF32::Params p{out, ldo, x.rows, w.n};
+    return run_gemm_sp<SpF32>(w, x, x.rows, ascale, p, st);
+}
+
+int launch_qkv_sp(const Operand &h, const SparseW &w, float ascale, int rows, uint8_t *q8, uint8_t *k8, uint8_t *v8,
+                  const float *cs, float cq, float ck, float cv, cudaStream_t st)
+{
+    SpQKV::Params p{q8, k8, v8, (const float2 *)cs, cq, ck, cv, rows};
+    return run_gemm_sp<SpQKV>(w, h, rows, ascale, p, st);
+}
+
+// The fp16 residual as the target of the sparse kernels' reduce-adds: boxes of 32 halves x 112 rows, unswizzled.
+static int sp_resid_map(CUtensorMap *m, __half *x, int rows)
+{
+    return make_tmap_2d_typed(m, x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, (uint64_t)rows, D * 2, 32, SP_COLS,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+int launch_oproj_sp(const Operand &a, const SparseW &w, float ascale, int rows, __half *x, cudaStream_t st)
+{
+    CUtensorMap xm;
+    if (sp_resid_map(&xm, x, rows)) return -1;
+    SpResid<false>::Params p{nullptr, nullptr, nullptr, rows};
+    return run_gemm_sp<SpResid<false>>(w, a, rows, ascale, p, st, &xm);
+}
+
+int launch_fc1_sp(const Operand &h, const SparseW &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
+                  cudaStream_t st)
+{
+    CUtensorMap hm;  // h8 [rows][2736] E4M3, stored in boxes of 16 units x 112 rows
+    if (make_tmap_2d(&hm, h8, HIDP, (uint64_t)rows, HIDP, 16, SP_COLS, CU_TENSOR_MAP_SWIZZLE_NONE)) return -1;
+    SpFC1::Params p{stat, rs, rows};
+    return run_gemm_sp<SpFC1>(w, h, rows, ascale, p, st, &hm);
+}
+
+int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
+                  const float *d, cudaStream_t st)
+{
+    CUtensorMap xm;
+    if (sp_resid_map(&xm, x, rows)) return -1;
+    k_rowstat<<<(rows + 255) / 256, 256, 0, st>>>(stat, rows);
+    XTB_CK(cudaGetLastError());
+    SpResid<true>::Params p{stat, c, d, rows};
+    return run_gemm_sp<SpResid<true>>(w, h8, rows, ascale, p, st, &xm);
+}
+
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
                    float qs_head, cudaStream_t st)
 {
@@ -283,6 +384,11 @@ int prepare_kernels()
                          (const void *)k_gemm<EpiHead<32>, 64, false, true, true>};
     for (const void *k : g64)
         if (set_smem(k, GemmCfg<64>::SMEM)) return -1;
+    const void *sp[] = {(const void *)k_gemm_sp<SpF32>, (const void *)k_gemm_sp<SpQKV>,
+                        (const void *)k_gemm_sp<SpResid<false>>, (const void *)k_gemm_sp<SpResid<true>>,
+                        (const void *)k_gemm_sp<SpFC1>};
+    for (const void *k : sp)
+        if (set_smem(k, SpCfg::SMEM)) return -1;
     return set_smem((const void *)k_attention, ATT_SMEM);
 }
 

@@ -70,6 +70,32 @@ int launch_head_f16(const Operand &hw, const Operand &pn, int nimg, int nt, cons
 int launch_head_e4m3(const Weight8 &hw, const Operand &pn8, float ascale, int nimg, int nt, const float *hb, float *out,
                      cudaStream_t st);
 
+// ---- 2:4-sparse projections (gemm_sp.cuh, tcgen05.mma.sp) ----
+// Weight compressed by sparse24_compress: values [np][kp / 2] (64-byte x 128-row boxes, 64B swizzle) and metadata
+// [np][kp / 8] (16-byte x 128-row boxes), np / kp = n / k rounded up to 128, plus the dense block scales.
+struct SparseW {
+    CUtensorMap va, me;
+    const float *ws;
+    int n, k, np, kp;
+};
+// Box height of the activation operand of the sparse kernels (tokens per tile).
+constexpr int SP_BOX_ROWS = 224;
+// 1 if every group of four consecutive k of every row holds at most two nonzero E4M3 codes (k a multiple of 4).
+int sparse24_check(const uint8_t *w, int n, int k);
+// Bytes of the compressed form (values, then metadata at *meta_off).
+size_t sparse24_bytes(int n, int k, size_t *meta_off);
+// Host memory in and out; -1 (with a stderr line) if w is not 2:4.
+int sparse24_compress(const uint8_t *w, int n, int k, uint8_t *vals, uint8_t *meta);
+int make_sparse_weight(SparseW *w, const uint8_t *vals, const uint8_t *meta, int n, int k, const float *ws);
+int launch_gemm_sp_f32(const Operand &x, const SparseW &w, float ascale, float *out, int ldo, cudaStream_t st);
+int launch_qkv_sp(const Operand &h, const SparseW &w, float ascale, int rows, uint8_t *q8, uint8_t *k8, uint8_t *v8,
+                  const float *cs, float cq, float ck, float cv, cudaStream_t st);
+int launch_oproj_sp(const Operand &a, const SparseW &w, float ascale, int rows, __half *x, cudaStream_t st);
+int launch_fc1_sp(const Operand &h, const SparseW &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
+                  cudaStream_t st);
+int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
+                  const float *d, cudaStream_t st);
+
 int current_device();
 // Shared-memory opt-in of every kernel on the current device (call before any stream capture).
 int prepare_kernels();

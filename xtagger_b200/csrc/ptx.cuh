@@ -229,6 +229,28 @@ __device__ __forceinline__ void umma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T with A 2:4-sparse along K, kind::f8f6f4 (E4M3): per instruction K = 64
+// logical elements, of which A holds the two kept bytes of every group of four (32 bytes per row) and the
+// metadata at TMEM column e_tmem (one row per lane, 4 bits per group: in-group index of the first kept element in
+// bits 0-1, of the second in bits 2-3; groups in K order, low nibble first; 2 columns per instruction) says where
+// they sit. e_tmem must be an even column.
+__device__ __forceinline__ void umma_sp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t e_tmem, uint32_t idesc,
+                                        uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f8f6f4 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Shared memory -> TMEM: 128 rows of 16 bytes (row i to lane i, 4 consecutive columns), asynchronous, ordered with
+// this thread's later tcgen05.mma and tracked by its tcgen05.commit.
+__device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc_)
+{
+    asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc_) : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -339,6 +361,18 @@ __device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t sbo_bytes,
     return d;
 }
 
+// Descriptor of an unswizzled tile of 16-byte rows stored back to back (8-row core matrices 128 bytes apart):
+// the source of tmem_cp_128x128b.
+__device__ __forceinline__ uint64_t sdesc_rows16(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((2048u >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((128u >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    return d;
+}
+
 // Instruction descriptor (kind::f8f6f4 with E4M3 operands, or kind::f16 with fp16 operands), fp32 accumulate,
 // both operands K-major, M = 128. Bits: [4,6) D format (1 = f32), [7,10) A format, [10,13) B format,
 // [15] A major, [16] B major, [17,23) N >> 3, [24,29) M >> 4.
@@ -346,6 +380,8 @@ __host__ __device__ constexpr uint32_t idesc_m128(uint32_t n)
 {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
+// The same with A 2:4-sparse (bit 2; K = 64 logical elements per instruction).
+__host__ __device__ constexpr uint32_t idesc_sp_m128(uint32_t n) { return idesc_m128(n) | (1u << 2); }
 // The same for a CTA-pair MMA of M = 256 (128 rows per CTA).
 __host__ __device__ constexpr uint32_t idesc_m256(uint32_t n)
 {

@@ -59,6 +59,13 @@ _SIGS = {
     "xtb_head_f16": (C.c_int, [_P, C.c_int, _P, C.c_int, _P, _P, _P]),
     "xtb_head_e4m3": (C.c_int, [_P, C.c_int, _P, _P, C.c_int, C.c_float, _P, _P, _P]),
     "xtb_fc2_noalloc": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
+    "xtb_sparse24_check": (C.c_int, [_P, C.c_int, C.c_int]),
+    "xtb_sparse24_compress": (C.c_int, [_P, C.c_int, C.c_int, _P, _P]),
+    "xtb_gemm_sp_e4m3_f32": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int, _P, C.c_float, _P, _P]),
+    "xtb_qkv_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P, _P, _P, C.c_float, C.c_float, C.c_float, _P]),
+    "xtb_oproj_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P]),
+    "xtb_fc1_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P, _P, _P]),
+    "xtb_fc2_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
     "xtb_error_word": (C.c_uint32, [C.c_int]),
     "xtb_error_clear": (None, [C.c_int]),
 }

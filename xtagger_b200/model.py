@@ -70,6 +70,22 @@ def interleave_gx(gx):
     return gx.reshape(2, HIDP // 16, 16, -1).transpose(1, 0, 2, 3).reshape(2 * HIDP, -1)
 
 
+def prune24_codes(q):
+    """2:4 selection by magnitude on E4M3 codes (prune24.py:44-56, "mag" mode): in every group of four consecutive
+    k of each row the two codes of smallest |value| become zero; among equal values the lower index is dropped first
+    (a stable sort, as numpy's argsort is for four elements). The scale of a 128 x 128 block is common to a group,
+    so ranking codes ranks the dequantised weights."""
+    q = np.ascontiguousarray(q, np.uint8)
+    n, k = q.shape
+    assert k % 4 == 0
+    v = np.abs(e4m3_decode(q)).reshape(n, k // 4, 4)
+    v[np.isnan(v)] = 0.0  # NaN codes score 0, as in prune24.py's E4 table
+    drop = np.argsort(v, axis=2, kind="stable")[:, :, :2]
+    keep = np.ones(v.shape, bool)
+    np.put_along_axis(keep, drop, False, axis=2)
+    return np.where(keep.reshape(n, k), q, 0).astype(np.uint8)
+
+
 def rope_table(theta=10000.0, grid=32, pt_seq=16):
     """EVA02 2D axial rotary table [1024][32][2] = (cos, sin) per patch token and rotary pair: pairs 0..15 rotate
     with the token's row coordinate, 16..31 with its column, frequencies theta^(-2i/32), coordinates scaled by
@@ -112,12 +128,14 @@ class _Blob:
         self.n += len(b)
 
 
-def write_synthetic(path, seed=0, nt=10861, nl=24, version=4, head_fp8=True, ln_noise=0.0, std=0.02):
+def write_synthetic(path, seed=0, nt=10861, nl=24, version=4, head_fp8=True, ln_noise=0.0, std=0.02, prune24=False):
     """Random-init EVA02-L tagger in eva02.bin format.
 
     Linears N(0, std) quantised to E4M3 (v4: per 128 x 128 block; v3: per tensor); LayerNorm gamma = 1 and
     beta = 0, perturbed by N(0, 0.1 ln_noise) when ln_noise > 0 (so that every folded term is exercised);
-    pos, cls, patch embedding N(0, std); EVA02 RoPE table; head bias 0.
+    pos, cls, patch embedding N(0, std); EVA02 RoPE table; head bias 0. prune24: the four projections of every
+    layer (QKV, O, W12, W2) made 2:4 sparse along k after quantisation (prune24_codes); the folded MLP term c is
+    computed from the pruned W2.
     Static activation scales: closed-form statistics of the random-init network, since LayerNorm outputs have
     unit variance per row: LN outputs amax 8; q / k / v amax 6 ||W row||_2 (max over rows); attention output
     bounded by v's; SwiGLU output 16 sigma_x sigma_g; every one times the reference's 1.25 headroom.
@@ -179,10 +197,14 @@ def write_synthetic(path, seed=0, nt=10861, nl=24, version=4, head_fp8=True, ln_
         for g, w in enumerate((wqkv, wo, w12, wt2)):
             if version == 4:
                 q, s = quant_blocks(w)
+                if prune24:
+                    q = prune24_codes(q)
                 table[i, g] = 1.0
                 mats.append((q, s, dequant_blocks(q, s)))
             else:
                 q, sc = quant_tensor(w)
+                if prune24:
+                    q = prune24_codes(q)
                 table[i, g] = sc
                 mats.append((q, None, e4m3_decode(q) * sc))
         rs = np.full(HIDP, 1.0 / table[i, 7], np.float32)  # raw h -> E4M3 operand (no smoothing)
