@@ -2,7 +2,10 @@
 split across N GPUs (one process per GPU, launched by torch.distributed.run for N > 1), random-init block-scaled
 E4M3 weights (24 layers, 10861 tags, FP8 head).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 64]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 64] [--nt 10861] [--sparse]
+
+--sparse is config 5: the four projections of every layer 2:4-pruned by magnitude (prune24.py's rule), which the
+engine runs on the sparse tensor cores (tcgen05.mma.sp); global batch 128 unless --batch is given.
 
 Prints one JSON line (rank 0):
   value       whole-job images/s with inputs resident on the devices (CUDA events around K graph launches on the
@@ -214,11 +217,15 @@ def run_ours(args, rank, world, local):
 
     # ---- roofline of the dominant kernel (fc1) from one direct forward with per-kernel events ----
     prof = eng.profile()
+    sparse_kinds = eng.sparse_kinds()
+    fc1_sparse = bool(sparse_kinds & 4)
     fc1_ms = prof["fc1"] / 24
     rows = nb * 1025
-    achieved = FC1_FLOP_PER_ROW * rows / (fc1_ms * 1e-3) / 1e12
+    achieved = FC1_FLOP_PER_ROW * rows / (fc1_ms * 1e-3) / 1e12   # dense-equivalent FLOPs
     bf16, peak_src = peaks()
-    peak = 2 * bf16
+    peak = (4 if fc1_sparse else 2) * bf16
+    if fc1_sparse:
+        peak_src = peak_src.replace("2x", "4x") + "; 2:4-sparse FP8 runs at twice the dense FP8 rate"
     out = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, dt = cpu_sample(model, nimg=4)
@@ -232,14 +239,19 @@ def run_ours(args, rank, world, local):
                 "config": {"workload": f"{config_name(args)}: EVA02-L 448^2 forward (24 layers, d 1024, 1025 tokens, {args.nt}-tag "
                                        "FP8 head), global batch split across the GPUs",
                            "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
-                           "weights": "random-init, E4M3 with fp32 scales per 128x128 block",
+                           "weights": "random-init, E4M3 with fp32 scales per 128x128 block" +
+                                      (", QKV / O / W12 / W2 2:4-pruned by magnitude" if args.sparse else ""),
+                           "sparse_kinds": sparse_kinds,
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
                 "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": args.batch * 1024 * 592 * 2,
                         "d2h_bytes_per_step": args.batch * args.nt * 4},
-                "roofline": {"bound": "tensor", "kernel": "fc1 (tcgen05 E4M3 GEMM + SwiGLU epilogue)",
+                "roofline": {"bound": "tensor",
+                             "kernel": "fc1 (tcgen05.mma.sp 2:4-sparse E4M3 GEMM + SwiGLU epilogue)" if fc1_sparse
+                             else "fc1 (tcgen05 E4M3 GEMM + SwiGLU epilogue)",
                              "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                              "peak_source": peak_src, "flop_per_launch": FC1_FLOP_PER_ROW * rows,
-                             "launch_ms": fc1_ms, "traffic": FC1_TRAFFIC_PER_ROW * rows,
+                             "launch_ms": fc1_ms,
+                             "traffic": None if fc1_sparse else FC1_TRAFFIC_PER_ROW * rows,
                              "traffic_unit": "bytes per launch (ncu DRAM read + write at batch 32, scaled by rows)"},
                 "forward_tflops": FLOP_PER_IMAGE * value / 1e12,
                 "profile_ms": prof,
@@ -253,7 +265,10 @@ def run_ours(args, rank, world, local):
 
 
 def config_name(args):
-    """The benchmark-plan config a run corresponds to (2: batch 1; 3: batch 64; 4: batch 32 with 13461 tags)."""
+    """The benchmark-plan config a run corresponds to (2: batch 1; 3: batch 64; 4: batch 32 with 13461 tags;
+    5: 2:4-sparse projections)."""
+    if args.sparse:
+        return "config 5"
     if args.nt == NT and args.batch == 1:
         return "config 2"
     if args.nt == NT and args.batch == 64:
@@ -269,12 +284,17 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=None, help="global batch (default 64; 128 with --sparse)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
+    ap.add_argument("--sparse", action="store_true", help="config 5: 2:4-pruned projections on the sparse kernels")
     args = ap.parse_args()
     rank, world, local = dist_env()
     MODEL_KW["nt"] = args.nt
+    if args.batch is None:
+        args.batch = 128 if args.sparse else 64
+    if args.sparse:
+        MODEL_KW["prune24"] = True
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -33,10 +33,14 @@ def models(tmp_path_factory):
         "v4_l2_h16": M.write_synthetic(os.path.join(d, "b.bin"), seed=6, nl=2, ln_noise=1.0, head_fp8=False),
         "v4_l24_h8": M.write_synthetic(os.path.join(d, "c.bin"), seed=0, nl=24, head_fp8=True),
         "v3_l24": M.write_synthetic(os.path.join(d, "d.bin"), seed=7, nl=24, version=3, head_fp8=False),
+        # 2:4-pruned projections (config 5): the engine runs them on the sparse tensor-core kernels
+        "v4_l2_p": M.write_synthetic(os.path.join(d, "e.bin"), seed=8, nl=2, ln_noise=1.0, head_fp8=True, prune24=True),
+        "v4_l24_p": M.write_synthetic(os.path.join(d, "f.bin"), seed=9, nl=24, head_fp8=True, prune24=True),
     }
 
 
-@pytest.mark.parametrize("name,nimg", [("v4_l2_h8", 3), ("v4_l2_h16", 2), ("v4_l24_h8", 1), ("v3_l24", 1)])
+@pytest.mark.parametrize("name,nimg", [("v4_l2_h8", 3), ("v4_l2_h16", 2), ("v4_l24_h8", 1), ("v3_l24", 1),
+                                       ("v4_l2_p", 3), ("v4_l24_p", 1)])
 def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     from oracle import oracle as O
     from xtagger_b200 import model as M
@@ -49,6 +53,7 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     eng = Engine(models[name], nb=max(nimg, 2))
     try:
         got = eng.run(x)
+        assert eng.sparse_kinds() == (15 if name.endswith("_p") else 0)
     finally:
         eng.close()
     assert xlib.xtb_error_word(0) == 0
@@ -61,6 +66,29 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     assert err.mean() <= max(2e-4, 1.5 * floor_mean)
     band = np.abs(want - THRESH) > tol_max
     assert ((got > THRESH) == (want > THRESH))[band].all()
+
+
+def test_sparse_engine_matches_dense_engine(xlib, cuda, models):
+    """The same pruned 2-layer model through the sparse kernels and (XTB_SPARSE=0) through the dense ones: the same
+    products in another fp32 summation order, so scores agree far inside the oracle tolerance."""
+    from xtagger_b200 import model as M
+    from xtagger_b200.engine import Engine
+    x = M.synthetic_inputs(3, seed=25)
+    out = {}
+    for mode in ("1", "0"):
+        os.environ["XTB_SPARSE"] = mode
+        try:
+            eng = Engine(models["v4_l2_p"], nb=3)
+            try:
+                out[mode] = eng.run(x)
+                assert eng.sparse_kinds() == (15 if mode == "1" else 0)
+            finally:
+                eng.close()
+        finally:
+            del os.environ["XTB_SPARSE"]
+    err = np.abs(out["1"] - out["0"])
+    print(f"sparse vs dense engine: max {err.max():.2e} mean {err.mean():.2e}")
+    assert err.max() <= 2e-3 and err.mean() <= 2e-4
 
 
 def test_teacher_forced_layers(xlib, cuda, models):

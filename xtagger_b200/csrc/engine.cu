@@ -8,6 +8,9 @@
 // scores (and head inputs), event; eva_wait sleeps on the events. Multi-GPU: one replica per device with its own
 // stream and graph; a submit's inputs are split into contiguous shards, one per device, and the scores land in
 // disjoint rows of one host slot. No collective is involved.
+// 2:4-sparse weights (prune24.py's output, or a block-scaled file pruned the same way): every projection kind whose
+// weights are 2:4 along k in all layers is compressed at bring-up and runs on the sparse tensor cores
+// (tcgen05.mma.sp, gemm_sp.cuh) with the same results; XTB_SPARSE=0 in the environment keeps the dense kernels.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -33,6 +36,7 @@ constexpr int NG = 4;  // block GEMMs per layer: QKV, O, W12, W2
 struct Layer {
     const float *ln1w, *ln1b, *ln2w, *ln2b, *rs, *c, *d;
     Weight8 w[NG];
+    SparseW sw[NG];  // kinds in Impl::sp_mask: the compressed weight
     float adq[NG], cq, ck, cv, sinv, vo;
 };
 
@@ -57,6 +61,8 @@ struct Replica {
     const float *pos = nullptr, *cs = nullptr, *fnw = nullptr, *fnb = nullptr;
     std::vector<Layer> L;
     Operand op_in, op_pe, op_h, op_h8, op_hw, op_pn;
+    Operand op_h_sp, op_h8_sp;     // the same activations in the sparse kernels' token boxes
+    uint8_t *spw = nullptr;        // compressed 2:4 weights (Impl::sp_host on this device)
     Weight8 whead;
     Attn attn;
     cudaGraphExec_t graph = nullptr;   // the forward reading input buffer 0 (in)
@@ -89,6 +95,12 @@ struct Impl {
     bool pool_reg = false, out_reg = false;
     uint32_t extra = 0;
     std::vector<float> hws_host;   // FP8 head block scales (host copy, for eva_head_put)
+    // 2:4-sparse projections: bit g set = kind g (QKV, O, W12, W2) runs on the sparse kernels; the compressed
+    // weights of every layer in one host buffer (layer i, kind g at sp_off[i * NG + g]; metadata after the values)
+    int sp_mask = 0;
+    bool sp_ready = false;
+    std::vector<uint8_t> sp_host;
+    std::vector<size_t> sp_off;
     uint32_t last_n = 0;
 };
 
@@ -276,17 +288,22 @@ int forward(Impl *im, Replica &r, eva *e, Prof *p)
         Layer &L = r.L[i];
         RCK(launch_ln_e4m3(r.x, L.ln1w, L.ln1b, r.h, rows, 1.0f / L.adq[0], st));
         RCK(record(p, st, P_LN1));
-        RCK(launch_qkv(r.op_h, L.w[0], L.adq[0], rows, r.q8, r.k8, r.v8, r.cs, L.cq, L.ck, L.cv, st));
+        const int sm = im->sp_mask;
+        if (sm & 1) RCK(launch_qkv_sp(r.op_h_sp, L.sw[0], L.adq[0], rows, r.q8, r.k8, r.v8, r.cs, L.cq, L.ck, L.cv, st));
+        else RCK(launch_qkv(r.op_h, L.w[0], L.adq[0], rows, r.q8, r.k8, r.v8, r.cs, L.cq, L.ck, L.cv, st));
         RCK(record(p, st, P_QKV));
         RCK(launch_attention(r.attn, nb, r.h, L.sinv, L.vo, st));
         RCK(record(p, st, P_ATTN));
-        RCK(launch_oproj(r.op_h, L.w[1], L.adq[1], rows, r.x, st));
+        if (sm & 2) RCK(launch_oproj_sp(r.op_h_sp, L.sw[1], L.adq[1], rows, r.x, st));
+        else RCK(launch_oproj(r.op_h, L.w[1], L.adq[1], rows, r.x, st));
         RCK(record(p, st, P_OPROJ));
         RCK(launch_ln_e4m3(r.x, L.ln2w, L.ln2b, r.h, rows, 1.0f / L.adq[2], st));
         RCK(record(p, st, P_LN2));
-        RCK(launch_fc1(r.op_h, L.w[2], L.adq[2], rows, r.h8, r.stat, L.rs, st));
+        if (sm & 4) RCK(launch_fc1_sp(r.op_h_sp, L.sw[2], L.adq[2], rows, r.h8, r.stat, L.rs, st));
+        else RCK(launch_fc1(r.op_h, L.w[2], L.adq[2], rows, r.h8, r.stat, L.rs, st));
         RCK(record(p, st, P_FC1));
-        RCK(launch_fc2(r.op_h8, L.w[3], L.adq[3], rows, r.x, r.stat, L.c, L.d, st));
+        if (sm & 8) RCK(launch_fc2_sp(r.op_h8_sp, L.sw[3], L.adq[3], rows, r.x, r.stat, L.c, L.d, st));
+        else RCK(launch_fc2(r.op_h8, L.w[3], L.adq[3], rows, r.x, r.stat, L.c, L.d, st));
         RCK(record(p, st, P_FC2));
         n += 9;  // ln1, qkv, attention (2), oproj, ln2, fc1, fc2 (row statistics + GEMM)
     }
@@ -297,6 +314,50 @@ int forward(Impl *im, Replica &r, eva *e, Prof *p)
     n++;
     RCK(record(p, st, P_HEAD));
     r.launches = n;
+    return 0;
+}
+
+// Which projection kinds are 2:4 in every layer, and their compressed form (once per engine, from the host blob;
+// r is the first replica, whose layout gives the weight offsets). Layers are compressed on parallel threads.
+int sparse_prepare(Impl *im, Replica &r, const uint8_t *hostblob)
+{
+    im->sp_ready = true;
+    const char *env = getenv("XTB_SPARSE");
+    if (env && env[0] == '0') return 0;
+    auto host_w = [&](int i, int g) { return hostblob + ((const uint8_t *)r.L[i].w[g].op.ptr - r.wts); };
+    for (int g = 0; g < NG; g++) {
+        bool all = true;
+        for (int i = 0; i < im->nl && all; i++) all = sparse24_check(host_w(i, g), r.L[i].w[g].n, r.L[i].w[g].k) != 0;
+        if (all) im->sp_mask |= 1 << g;
+    }
+    if (!im->sp_mask) return 0;
+    im->sp_off.assign((size_t)im->nl * NG, 0);
+    size_t total = 0;
+    for (int i = 0; i < im->nl; i++)
+        for (int g = 0; g < NG; g++)
+            if (im->sp_mask & (1 << g)) {
+                im->sp_off[(size_t)i * NG + g] = total;
+                total += (sparse24_bytes(r.L[i].w[g].n, r.L[i].w[g].k, nullptr) + 255) & ~(size_t)255;
+            }
+    im->sp_host.resize(total);
+    const int nthr = std::max(1, std::min(im->nl, 8));
+    std::vector<std::thread> th;
+    std::vector<int> rcs(nthr, 0);
+    for (int t = 0; t < nthr; t++)
+        th.emplace_back([&, t] {
+            for (int i = t; i < im->nl; i += nthr)
+                for (int g = 0; g < NG; g++)
+                    if (im->sp_mask & (1 << g)) {
+                        const int n = r.L[i].w[g].n, k = r.L[i].w[g].k;
+                        size_t moff = 0;
+                        sparse24_bytes(n, k, &moff);
+                        uint8_t *v = im->sp_host.data() + im->sp_off[(size_t)i * NG + g];
+                        if (sparse24_compress(host_w(i, g), n, k, v, v + moff)) rcs[t] = -1;
+                    }
+        });
+    for (auto &x : th) x.join();
+    for (int rc : rcs)
+        if (rc) return -1;
     return 0;
 }
 
@@ -311,6 +372,21 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     int off = layout(im, r, hostblob);
     if (off < 0) return -1;
     RCK(head_layout(im, r, e, (size_t)off));
+    if (!im->sp_ready) RCK(sparse_prepare(im, r, hostblob));
+    if (im->sp_mask) {
+        ECK(cudaMalloc(&r.spw, im->sp_host.size()));
+        ECK(cudaMemcpyAsync(r.spw, im->sp_host.data(), im->sp_host.size(), cudaMemcpyHostToDevice, r.st));
+        for (int i = 0; i < im->nl; i++)
+            for (int g = 0; g < NG; g++)
+                if (im->sp_mask & (1 << g)) {
+                    Layer &L = r.L[i];
+                    size_t moff = 0;
+                    sparse24_bytes(L.w[g].n, L.w[g].k, &moff);
+                    const uint8_t *v = r.spw + im->sp_off[(size_t)i * NG + g];
+                    RCK(make_sparse_weight(&L.sw[g], v, v + moff, L.w[g].n, L.w[g].k, L.w[g].ws));
+                }
+        ECK(cudaStreamSynchronize(r.st));  // the host buffer is pageable
+    }
     const int nb = r.nb, rows = nb * T;
     // head used by the forward: the blob's rows, or a copy with the extra rows (zero weights, bias -16)
     const uint32_t nt = e->nt, nt0 = e->nt0;
@@ -361,6 +437,8 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     RCK(make_operand(&r.op_pe, r.pe, D, K0P * 2, 256));
     RCK(make_operand(&r.op_h, r.h, rows, D, 128));
     RCK(make_operand(&r.op_h8, r.h8, rows, HIDP, 128));
+    RCK(make_operand(&r.op_h_sp, r.h, rows, D, SP_BOX_ROWS));
+    RCK(make_operand(&r.op_h8_sp, r.h8, rows, HIDP, SP_BOX_ROWS));
     if (im->head8) {
         r.whead.ws = r.hws;
         r.whead.n = (int)nt;
@@ -746,7 +824,7 @@ void eva_close(eva *e)
             if (r.in_ready[k]) cudaEventDestroy(r.in_ready[k]);
             if (r.in_free[k]) cudaEventDestroy(r.in_free[k]);
         }
-        void *bufs[] = {r.in, r.in_b, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp};
+        void *bufs[] = {r.in, r.in_b, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp, r.spw};
         for (void *p : bufs)
             if (p) cudaFree(p);
         if (r.head_copy) {
@@ -818,6 +896,12 @@ void *eva_stream(eva *e, int i)
     Impl *im = I(e);
     if (!im || eva_ready(e) || i < 0 || (size_t)i >= im->reps.size()) return nullptr;
     return (void *)im->reps[i].st;
+}
+
+int eva_sparse_kinds(eva *e)
+{
+    if (eva_ready(e)) return -1;
+    return I(e)->sp_mask;
 }
 
 int eva_launches_per_forward(eva *e)

@@ -101,6 +101,10 @@ class Engine:
     def launches_per_forward(self):
         return self.lib.eva_launches_per_forward(C.byref(self.e))
 
+    def sparse_kinds(self):
+        """Bit mask of the projections on the 2:4-sparse kernels (1 QKV, 2 O, 4 W12, 8 W2)."""
+        return self.lib.eva_sparse_kinds(C.byref(self.e))
+
     def profile(self):
         ms = np.zeros(16, np.float32)
         k = self.lib.eva_profile(C.byref(self.e), ms.ctypes.data_as(C.c_void_p), 16)

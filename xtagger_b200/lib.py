@@ -45,6 +45,7 @@ _SIGS = {
     "eva_download": (C.c_int, [C.POINTER(Eva), _P, C.c_uint32]),
     "eva_stream": (_P, [C.POINTER(Eva), C.c_int]),
     "eva_launches_per_forward": (C.c_int, [C.POINTER(Eva)]),
+    "eva_sparse_kinds": (C.c_int, [C.POINTER(Eva)]),
     "eva_profile": (C.c_int, [C.POINTER(Eva), _P, C.c_int]),
     "eva_prof_name": (C.c_char_p, [C.c_int]),
     "xtb_gemm_e4m3_f32": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_float, _P, _P]),
