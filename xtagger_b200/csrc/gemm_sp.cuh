@@ -1,7 +1,7 @@
 // 2:4-sparse block-scaled FP8 GEMM on tcgen05.mma.sp (sm_100a), the weights as the sparse operand:
 //     D[n][t] = epilogue( sum_k W[n][k] * X[t][k] )        n: weight row (output feature), t: token
 // tcgen05 takes sparsity on the A operand only, so the weights are A (128 rows per tile, one per TMEM lane) and the
-// activations are B (SP_BT = 224 tokens per tile, TMEM columns): the accumulator holds the transposed output. The
+// activations are B (SP_BT = 112 tokens per tile, TMEM columns): the accumulator holds the transposed output. The
 // epilogues below are the transposed forms of those in epilogues.cuh, with the same arithmetic per (token,
 // feature), so that on pruned weights this path reproduces the dense one (the reference runs pruned weights,
 // prune24.py's output, through its dense kernels: this is the same product on the sparse tensor-core path).
@@ -14,36 +14,39 @@
 // 128 k, 2 columns per K = 64 instruction.
 //
 // Pipeline stage = one 128-element K block (one block scale): 128 weight rows x 64 value bytes (64B swizzle),
-// 128 x 16 metadata bytes (unswizzled), 224 tokens x 128 activation bytes (128B swizzle).
+// 128 x 16 metadata bytes (unswizzled), 112 tokens x 128 activation bytes (128B swizzle).
 // Warps (320 threads): 0 TMA producer; 1 TMEM allocation and MMA issue (tcgen05.cp of the stage's metadata into
-// TMEM, then two K = 64 sparse MMAs); 2..9 epilogue: warp w reads TMEM lanes 32 (w % 4) .. (32 features) and the
-// token half (w - 2) / 4 of the tile (112 columns), promoting the block scales per K block as gemm.cuh does.
-// TMEM: accumulators at columns [0, 224) and [224, 448) (ping-pong per K block), metadata at 448 and 452
-// (ping-pong per K block; a metadata column must be even).
+// TMEM, then two K = 64 sparse MMAs); 2..9 epilogue, as two groups of four warps (one per TMEM lane quadrant,
+// warp w reads lanes 32 (w % 4) ..) that take the CTA's tiles in turn: while one group runs a tile's epilogue (the
+// fused apply phase, from registers), the MMA fills the other group's accumulators, so the apply overlaps the main
+// loop instead of stalling it. Block scales are promoted per K block as gemm.cuh does.
+// TMEM: four accumulators of 112 columns (group g: 2g and 2g + 1, ping-pong per K block) at [0, 448), metadata at
+// 448 and 452 (ping-pong per K block; a metadata column must be even).
 #pragma once
 #include "gemm.cuh"
 #include "ops.h"
 
 namespace xtb {
 
-constexpr int SP_BT = 224;          // tokens per tile (MMA N)
-constexpr int SP_COLS = SP_BT / 2;  // token columns per epilogue thread
+constexpr int SP_BT = 112;          // tokens per tile (MMA N)
+constexpr int SP_COLS = SP_BT;      // token columns per epilogue thread (a group's four warps cover a tile)
 
 struct SpCfg {
     static constexpr int A_BYTES = 128 * 64;
     static constexpr int E_BYTES = 128 * 16;
     static constexpr int B_BYTES = SP_BT * 128;
     static constexpr int STAGE_BYTES = A_BYTES + E_BYTES + B_BYTES;
-    static constexpr int STAGES = 4;
+    static constexpr int STAGES = 6;
     static constexpr int EW = 8;
-    static constexpr int STAGE_PER_WARP = SP_COLS * 64;      // 112 tokens x 32 fp16 features
-    static constexpr int XRED_FLOAT2 = 2 * 2 * 4 * SP_COLS;  // fc1 statistics exchange [half][buffer][quad][token]
-    static constexpr int E_COL = 2 * SP_BT;                  // metadata TMEM columns (two buffers of 4)
+    static constexpr int STAGE_PER_WARP = SP_COLS * 64;      // epilogue scratch per warp: 112 tokens x 64 bytes
+    static constexpr int XRED_FLOAT2 = 2 * 2 * 4 * SP_COLS;  // fc1 statistics exchange [group][buffer][quad][token]
+    static constexpr int E_COL = 4 * SP_BT;                  // metadata TMEM columns (two buffers of 4)
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + EW * STAGE_PER_WARP + XRED_FLOAT2 * 8 + 256;
     static constexpr int THREADS = 64 + 32 * EW;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(E_COL + 8 <= 512, "TMEM budget");
     static_assert(SP_COLS % 16 == 0, "epilogue drains 16 columns at a time");
+    static_assert(B_BYTES % 1024 == 0, "128B-swizzled stages stay 1024-byte aligned");
 };
 
 struct SpArgs {
@@ -59,12 +62,18 @@ struct SpArgs {
 // Epilogue context of one thread: weight row (feature) f0 + lane, tokens t0 .. t0 + SP_COLS - 1.
 struct SpCtx {
     int f0, t0, nb, lane, quad;
-    uint8_t *stage;            // this warp's staging buffer (STAGE_PER_WARP bytes)
-    float2 *xred;              // this token half's exchange buffers [2][4][SP_COLS]
-    uint64_t *xbar;            // their barriers [2] (one arrival per warp of the half)
-    uint32_t xuse;             // exchanges done by this warp
+    uint8_t *stage;            // this warp's scratch (STAGE_PER_WARP bytes)
+    uint8_t *gscratch;         // this group's scratch (its four warps' slices, contiguous)
+    float2 *xred;              // this group's exchange buffers [2][4][SP_COLS]
+    uint64_t *ebar;            // this group's four epilogue barriers (meaning set by the epilogue)
+    uint32_t use;              // epilogue-defined counter (exchanges / prefetches done by this warp)
     const CUtensorMap *tmC;
     uint32_t *err;
+};
+
+// Epilogues without barriers or per-tile prefetch.
+struct SpNoBars {
+    __device__ __forceinline__ static void init_bars(uint64_t *) {}
 };
 
 template <class Epi>
@@ -79,16 +88,16 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = smem;                       // weight values: 64B-swizzle atoms (512 bytes) need 512-byte alignment
-    uint8_t *sB = sA + STAGES * C::A_BYTES;   // activations: 128B swizzle, 1024-byte aligned (28 KB per stage)
+    uint8_t *sB = sA + STAGES * C::A_BYTES;   // activations: 128B swizzle, 1024-byte aligned (14 KB per stage)
     uint8_t *sE = sB + STAGES * C::B_BYTES;   // metadata
-    uint8_t *sStage = sE + STAGES * C::E_BYTES;
-    float2 *xred = (float2 *)(sStage + C::EW * C::STAGE_PER_WARP);
+    uint8_t *sEpi = sE + STAGES * C::E_BYTES;
+    float2 *xred = (float2 *)(sEpi + C::EW * C::STAGE_PER_WARP);
     uint64_t *full = (uint64_t *)(xred + C::XRED_FLOAT2);
     uint64_t *empty = full + STAGES;
-    uint64_t *tfull = empty + STAGES;
-    uint64_t *tempty = tfull + 2;
-    uint64_t *xbar = tempty + 2;              // [half][buffer]
-    uint32_t *tslot = (uint32_t *)(xbar + 4);
+    uint64_t *tfull = empty + STAGES;         // [4] accumulators
+    uint64_t *tempty = tfull + 4;
+    uint64_t *ebar = tempty + 4;              // [group][4]
+    uint32_t *tslot = (uint32_t *)(ebar + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -96,11 +105,11 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < 4; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], C::EW);
+            mbar_init(&tempty[b], 4);  // the four warps of the group that owns the accumulator
         }
-        for (int b = 0; b < 4; b++) mbar_init(&xbar[b], 4);
+        Epi::init_bars(ebar);
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmE);
@@ -143,11 +152,14 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
     } else if (warp == 1) {
         if (elect_one()) {
             int stage = 0;
-            uint32_t ph = 0, tb = 0, tph = 0, eb = 0;
+            uint32_t ph = 0, eb = 0, cnt[2] = {0, 0};  // K blocks issued into each group's accumulators
             bool ok = true;
-            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+            for (int t = blockIdx.x, i = 0; t < total && ok; t += gridDim.x, i++) {
+                const int grp = i & 1;
                 for (int k = 0; k < KI; k++) {
-                    if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
+                    const uint32_t c = cnt[grp];
+                    const int buf = 2 * grp + (int)(c & 1);
+                    if (!(ok = mbar_wait(&tempty[buf], ((c >> 1) & 1) ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
                     tc_fence_after();
                     if (!(ok = mbar_wait(&full[stage], ph, g.err, XTB_ERR_WAIT_TMA))) break;
                     tc_fence_after();
@@ -155,15 +167,15 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
                     tmem_cp_128x128b(ecol, sdesc_rows16(smem_u32(sE + stage * C::E_BYTES)));
                     const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
-                    const uint32_t d = tbase + tb * SP_BT;
+                    const uint32_t d = tbase + buf * SP_BT;
 #pragma unroll
                     for (int kk = 0; kk < 2; kk++)
                         umma_sp(d, sdesc(a0 + kk * 32, 512, SWZ_64B), sdesc(b0 + kk * 64, 1024, SWZ_128B), ecol + 2 * kk,
                                 IDESC, kk > 0);
                     umma_commit(&empty[stage]);
-                    umma_commit(&tfull[tb]);
+                    umma_commit(&tfull[buf]);
                     eb ^= 1;
-                    if ((tb ^= 1) == 0) tph ^= 1;
+                    cnt[grp] = c + 1;
                     if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1;
@@ -174,53 +186,56 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
     } else {
         const int ew = warp - 2;
         const int quad = warp & 3;
-        const int half = ew >> 2;  // which 112-token half of the tile
+        const int grp = ew >> 2;  // epilogue group: tiles grp, grp + 2, ... of this CTA
         SpCtx cx;
         cx.lane = lane;
         cx.quad = quad;
-        cx.stage = sStage + ew * C::STAGE_PER_WARP;
-        cx.xred = xred + half * (2 * 4 * SP_COLS);
-        cx.xbar = xbar + 2 * half;
-        cx.xuse = 0;
+        cx.stage = sEpi + ew * C::STAGE_PER_WARP;
+        cx.gscratch = sEpi + grp * 4 * C::STAGE_PER_WARP;
+        cx.xred = xred + grp * (2 * 4 * SP_COLS);
+        cx.ebar = ebar + 4 * grp;
+        cx.use = 0;
         cx.tmC = &tmC;
         cx.err = g.err;
-        uint32_t tb = 0, tph = 0;
+        uint32_t c = 0;  // K blocks drained by this group
         bool ok = true;
-        for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        for (int t = blockIdx.x + grp * gridDim.x; t < total && ok; t += 2 * gridDim.x) {
             const int nb = t % g.n_tiles, tt = t / g.n_tiles;
             cx.nb = nb;
             cx.f0 = nb * 128 + quad * 32;
-            cx.t0 = tt * SP_BT + half * SP_COLS;
+            cx.t0 = tt * SP_BT;
+            if (!(ok = Epi::begin(ep, cx))) break;  // per-tile loads issued before the accumulator is ready
             float2 acc[SP_COLS / 2];
 #pragma unroll
             for (int j = 0; j < SP_COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);
             const float *wsr = g.ws + (size_t)min(nb, g.ws_rows - 1) * g.ws_ld;
             float snext = __ldg(wsr);
             const float amul = g.ascale * Epi::row_scale(ep, cx.f0);
-            for (int u = 0; u < KI; u++) {
+            for (int u = 0; u < KI; u++, c++) {
                 const float s = amul * snext;
                 if (u + 1 < KI) snext = __ldg(wsr + u + 1);
-                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
+                const int buf = 2 * grp + (int)(c & 1);
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[buf], (c >> 1) & 1, g.err, XTB_ERR_WAIT_TMEM)))) break;
                 tc_fence_after();
-                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * SP_BT + half * SP_COLS;
+                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + buf * SP_BT;
                 const float2 s2 = make_float2(s, s);
 #pragma unroll
-                for (int c = 0; c < SP_COLS / 16; c++) {
+                for (int cc = 0; cc < SP_COLS / 16; cc++) {
                     float v[16];
-                    tmem_ld16(taddr + c * 16, v);
+                    tmem_ld16(taddr + cc * 16, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 8; j++) acc[c * 8 + j] = ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[c * 8 + j]);
+                    for (int j = 0; j < 8; j++) acc[cc * 8 + j] = ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[cc * 8 + j]);
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[tb]);
-                if ((tb ^= 1) == 0) tph ^= 1;
+                if (lane == 0) mbar_arrive(&tempty[buf]);
             }
             if (!ok) break;
             ok = Epi::apply(ep, (const float *)acc, cx);
         }
-        if (lane == 0) bulk_wait0();  // the epilogue's TMA stores / reductions have completed
+        asm volatile("cp.async.wait_all;" ::: "memory");  // no copy of an abandoned prefetch outlives the CTA
+        if (lane == 0) bulk_wait0();                        // the epilogue's TMA stores / reductions have completed
         __syncwarp();
     }
     __syncthreads();
@@ -232,18 +247,20 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Transposed epilogues: apply(params, acc[SP_COLS], ctx); acc[j] = output (token ctx.t0 + j, feature ctx.f0 + lane),
-// already dequantised. Tokens past M and features past the problem are skipped. Return false only when a bounded
-// wait ran out.
+// Transposed epilogues: begin(params, ctx) when a tile starts (before its accumulator is ready), apply(params,
+// acc[SP_COLS], ctx) when it is complete: acc[j] = output (token ctx.t0 + j, feature ctx.f0 + lane), already
+// dequantised. init_bars sets up the epilogue's barriers (four per group). Tokens past M and features past the
+// problem are skipped. begin / apply return false only when a bounded wait ran out.
 // ---------------------------------------------------------------------------------------------------------------
 
 // Plain fp32 store out[t][f] (row stride ld floats): the stand-alone sparse GEMM.
-struct SpF32 {
+struct SpF32 : SpNoBars {
     struct Params {
         float *out;
         int ld, M, N;
     };
     __device__ __forceinline__ static float row_scale(const Params &, int) { return 1.0f; }
+    __device__ __forceinline__ static bool begin(const Params &, SpCtx &) { return true; }
     __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
     {
         const int f = cx.f0 + cx.lane;
@@ -258,8 +275,12 @@ struct SpF32 {
 
 // QKV (k_qkv, eva_kernels.cu:41-114), as EpiQKV: q / k rows get the interleaved RoPE of patch tokens (dims 2j and
 // 2j + 1 are neighbouring lanes), v rows are only scaled (cq / ck / cv ride on the block-scale promotion); E4M3 into
-// q8 / k8 / v8 [img][head][TP][64]. A warp holds half a head (32 dims) for 112 tokens: bytes are staged as
-// [token][32] and leave as 16-byte pieces.
+// q8 / k8 / v8 [img][head][TP][64], one byte per lane (32 consecutive bytes per warp store).
+// The RoPE angles of the tile's 112 tokens for a warp's 16 dim pairs (14 KB, [token][16 pairs]) are copied into the
+// group's scratch by cp.async when the tile starts, so their latency hides behind the main loop. The two warps of
+// a group that hold the same dims of the two heads (quads q and q ^ 2) share one buffer, each copying half of the
+// tokens; group barriers 0 / 1 (64 arrivals: the copies of both warps' lanes have landed) and 2 / 3 (2 arrivals:
+// both warps have read the buffer) order each use of the buffer of dim half 0 / 1.
 struct SpQKV {
     struct Params {
         uint8_t *q8, *k8, *v8;
@@ -267,43 +288,70 @@ struct SpQKV {
         float cq, ck, cv;
         int M;
     };
+    __device__ __forceinline__ static void init_bars(uint64_t *eb)
+    {
+        for (int g = 0; g < 2; g++)
+            for (int h = 0; h < 2; h++) {
+                mbar_init(&eb[4 * g + h], 64);
+                mbar_init(&eb[4 * g + 2 + h], 2);
+            }
+    }
     __device__ __forceinline__ static float row_scale(const Params &p, int f0)
     {
         const int which = f0 >> 10;
         return which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
     }
+    __device__ __forceinline__ static uint8_t *angles(const SpCtx &cx) { return cx.gscratch + (cx.quad & 1) * (SP_COLS * 128); }
+    __device__ __forceinline__ static bool begin(const Params &p, SpCtx &cx)
+    {
+        if ((cx.f0 >> 10) == 2) return true;  // v rows: no RoPE
+        const int h = cx.quad & 1;
+        // the previous use of the buffer has been read by both warps
+        if (cx.use > 0 &&
+            !__all_sync(0xffffffffu, mbar_wait(&cx.ebar[2 + h], (cx.use - 1) & 1, cx.err, XTB_ERR_WAIT_TMEM)))
+            return false;
+        uint8_t *buf = angles(cx);
+        const int r0 = (cx.quad >> 1) * (SP_COLS / 2);  // quads 0 / 1 copy tokens 0..55, quads 2 / 3 tokens 56..111
+        const float2 *src = p.cs + ((cx.f0 & 63) >> 1);  // this warp's first pair (0 or 16)
+        for (int i = cx.lane; i < (SP_COLS / 2) * 8; i += 32) {
+            const int r = r0 + (i >> 3), ch = i & 7;
+            const int t = cx.t0 + r, tt = t % T;
+            if (t < p.M && tt > 0) cp_async16(buf + r * 128 + ch * 16, src + (size_t)(tt - 1) * 32 + ch * 2);
+        }
+        cp_async_mbar_arrive(&cx.ebar[h]);
+        return true;
+    }
     __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
     {
         const int which = cx.f0 >> 10, head = (cx.f0 & 1023) >> 6, dbase = cx.f0 & 63;
-        const int jp = (dbase + cx.lane) >> 1;  // RoPE pair of this lane's dim
+        const int h = cx.quad & 1;
         const bool odd = cx.lane & 1;
-        int tt = cx.t0 % T;
-        __syncwarp();  // the previous tile's copies out of the staging buffer are done
+        const uint8_t *ang = angles(cx) + (cx.lane >> 1) * 8;
+        if (which < 2 && !__all_sync(0xffffffffu, mbar_wait(&cx.ebar[h], cx.use & 1, cx.err, XTB_ERR_WAIT_TMEM)))
+            return false;
+        uint8_t *dst = (which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8) + dbase + cx.lane;
+        int b = cx.t0 / T, tt = cx.t0 - b * T;
 #pragma unroll
         for (int j = 0; j < SP_COLS; j++) {
             float v = acc[j];
+            const bool live = cx.t0 + j < p.M;
             if (which < 2) {
                 // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin); cls rows and rows past M: cos 1, sin 0
                 const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
                 float2 c = make_float2(1.f, 0.f);
-                if (tt > 0 && cx.t0 + j < p.M) c = __ldg(p.cs + (size_t)(tt - 1) * 32 + jp);
+                if (tt > 0 && live) c = *(const float2 *)(ang + j * 128);
                 v = fmaf(pv, odd ? c.y : -c.y, v * c.x);
             }
-            cx.stage[j * 32 + cx.lane] = (uint8_t)e4m3x2(v, 0.f);
-            if (++tt == T) tt = 0;
-        }
-        __syncwarp();
-        uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
-#pragma unroll
-        for (int i = 0; i < SP_COLS * 2 / 32; i++) {
-            const int pc = i * 32 + cx.lane;  // piece: token r, 16-byte half ch of its 32 dims
-            const int r = pc >> 1, ch = pc & 1;
-            const int t = cx.t0 + r;
-            if (t < p.M) {
-                const int b = t / T, tq = t - b * T;
-                *(uint4 *)(dst + (((size_t)(b * NH + head) * TP + tq) << 6) + dbase + 16 * ch) =
-                    *(const uint4 *)(cx.stage + r * 32 + 16 * ch);
+            if (live) dst[((size_t)(b * NH + head) * TP + tt) << 6] = (uint8_t)e4m3x2(v, 0.f);
+            if (++tt == T) {
+                tt = 0;
+                ++b;
             }
+        }
+        if (which < 2) {
+            __syncwarp();
+            if (cx.lane == 0) mbar_arrive(&cx.ebar[2 + h]);
+            cx.use++;
         }
         return true;
     }
@@ -314,13 +362,14 @@ struct SpQKV {
 // LayerNorm folded in (EpiFC2, LN = true: delta = rstd * (acc - mean * c[f]) + d[f] with (mean, rstd) of the token
 // from k_rowstat).
 template <bool LN>
-struct SpResid {
+struct SpResid : SpNoBars {
     struct Params {
         const float2 *ms;
         const float *c, *d;
         int M;
     };
     __device__ __forceinline__ static float row_scale(const Params &, int) { return 1.0f; }
+    __device__ __forceinline__ static bool begin(const Params &, SpCtx &) { return true; }
     __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
     {
         if (cx.lane == 0) bulk_wait_read0();  // the previous tile's reduction has read the staging buffer
@@ -379,14 +428,21 @@ __device__ __forceinline__ void halfwarp_sum8(float (&v)[8], int lane)
 // warp's lanes 0-15 hold g and lanes 16-31 x of the same 16 units: one exchange gives lanes 0-15 tokens 0..55 and
 // lanes 16-31 tokens 56..111 of (g, x). u = x g sigmoid(g), h8 = E4M3(u rs[unit]) stored by TMA (boxes of 16 units x
 // 112 tokens); the row statistics partial stat[nb][t] (sum u, sum u^2 over the tile's 64 units) is summed across
-// the 16 lanes, then across the four warps of the token half through shared memory.
+// the 16 lanes, then across the group's four warps through shared memory (group barriers 0 / 1, one per exchange
+// buffer, four arrivals).
 struct SpFC1 {
     struct Params {
         float2 *stat;
         const float *rs;
         int M;
     };
+    __device__ __forceinline__ static void init_bars(uint64_t *eb)
+    {
+        for (int g = 0; g < 2; g++)
+            for (int b = 0; b < 2; b++) mbar_init(&eb[4 * g + b], 4);
+    }
     __device__ __forceinline__ static float row_scale(const Params &, int) { return 1.0f; }
+    __device__ __forceinline__ static bool begin(const Params &, SpCtx &) { return true; }
     __device__ __forceinline__ static bool apply(const Params &p, const float *acc, SpCtx &cx)
     {
         constexpr int H = SP_COLS / 2;  // tokens per lane after the exchange
@@ -395,7 +451,7 @@ struct SpFC1 {
         const int unit = (cx.f0 >> 1) + (lane & 15);
         const bool live = cx.f0 < N12;  // warp-uniform: false for the padding rows of the last weight tile
         const float r = (live && unit < HIDP) ? __ldg(p.rs + unit) : 0.0f;
-        const uint32_t buf = cx.xuse & 1;
+        const uint32_t buf = cx.use & 1;
         float2 *xr = cx.xred + buf * 4 * SP_COLS;
         if (lane == 0) bulk_wait_read0();  // the previous tile's h8 store has read the staging buffer
         __syncwarp();
@@ -426,8 +482,8 @@ struct SpFC1 {
             tma_store_2d(cx.tmC, cx.stage, cx.f0 >> 1, cx.t0);
             bulk_commit();
         }
-        if (lane == 0) mbar_arrive(&cx.xbar[buf]);
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(&cx.xbar[buf], (cx.xuse >> 1) & 1, cx.err, XTB_ERR_WAIT_TMEM));
+        if (lane == 0) mbar_arrive(&cx.ebar[buf]);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(&cx.ebar[buf], (cx.use >> 1) & 1, cx.err, XTB_ERR_WAIT_TMEM));
         if (ok && lane < SP_COLS / 4) {
             const int tk = (SP_COLS / 4) * cx.quad + lane;
             float2 a = xr[tk];
@@ -440,7 +496,7 @@ struct SpFC1 {
             const int t = cx.t0 + tk;
             if (t < p.M) p.stat[(size_t)cx.nb * p.M + t] = a;
         }
-        cx.xuse++;
+        cx.use++;
         return ok;
     }
 };

@@ -79,7 +79,7 @@ struct SparseW {
     int n, k, np, kp;
 };
 // Box height of the activation operand of the sparse kernels (tokens per tile).
-constexpr int SP_BOX_ROWS = 224;
+constexpr int SP_BOX_ROWS = 112;
 // 1 if every group of four consecutive k of every row holds at most two nonzero E4M3 codes (k a multiple of 4).
 int sparse24_check(const uint8_t *w, int n, int k);
 // Bytes of the compressed form (values, then metadata at *meta_off).
