@@ -179,6 +179,19 @@ int xtb_fc1_sp(const uint8_t *h, int rows, const uint8_t *vals, const uint8_t *m
 int xtb_fc2_sp(const uint8_t *h8, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
                uint16_t *x, float *stat, const float *c, const float *d, void *stream);
 
+/* ---- GPU preprocessing (procimg.h's wd path: pi_ingest / pi_prep, done there on the host) ----
+ * A decoded image on the device: h rows of w RGBA (or RGBX) pixels, `stride` bytes apart (a multiple of 4, at least
+ * 4 w; 4-byte aligned). xtb_prep_ingest applies alpha over white in place when `alpha` (X = 255 either way) and
+ * builds the 2x2 box pyramid into `scratch`; xtb_prep_crop then writes the model input (EVA_IN halves, device
+ * pointer `out`) of the rect (x0, y0, cw, ch) of that image: resampled into a 448^2 white square with the
+ * antialiased bicubic (or only normalised when its long side is 448), [-1, 1] fp16, BGR planes, the patch operand
+ * layout. Outputs are bit-identical to the reference's arithmetic. scratch: xtb_prep_scratch_bytes(w, h) device
+ * bytes, owned by the caller, for one image at a time. Stream-ordered, no allocation. */
+size_t xtb_prep_scratch_bytes(int w, int h);
+int xtb_prep_ingest(uint8_t *rgba, int w, int h, int stride, int alpha, void *scratch, void *stream);
+int xtb_prep_crop(const uint8_t *rgba, int w, int h, int stride, int x0, int y0, int cw, int ch, void *scratch,
+                  uint16_t *out, void *stream);
+
 /* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). */
 uint32_t xtb_error_word(int device);
 void xtb_error_clear(int device);

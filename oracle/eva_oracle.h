@@ -66,4 +66,11 @@ int or_model_nt(const char *model);
 void or_prune24(uint8_t *w, int n, int k, int wanda);
 
 int or_threads(void);
+
+/* GPU preprocessing restated (prep_oracle.c; src/core/procimg.h's wd path) */
+uint32_t or_div255(uint32_t x);
+void or_over_white(uint8_t *img, int w, int h, int stride, int alpha);
+void or_half(const uint8_t *s, int sw, int sh, int sstride, uint8_t *d, int dstride);
+void or_prep(uint8_t *img, int w, int h, int stride, int alpha, int x0, int y0, int cw, int ch, uint16_t *out);
+int or_prep_level(int w, int h, int side);
 #endif

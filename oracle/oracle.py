@@ -53,6 +53,11 @@ def lib():
             "or_model_nt": (C.c_int, [C.c_char_p]),
             "or_prune24": (None, [_u8, C.c_int, C.c_int, C.c_int]),
             "or_threads": (C.c_int, []),
+            "or_div255": (C.c_uint32, [C.c_uint32]),
+            "or_over_white": (None, [_u8, C.c_int, C.c_int, C.c_int, C.c_int]),
+            "or_half": (None, [_u8, C.c_int, C.c_int, C.c_int, _u8, C.c_int]),
+            "or_prep": (None, [_u8, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _u16]),
+            "or_prep_level": (C.c_int, [C.c_int, C.c_int, C.c_int]),
         }
         for name, (res, args) in sig.items():
             f = getattr(l, name)

@@ -1,0 +1,65 @@
+"""GPU preprocessing (xtb_prep_ingest / xtb_prep_crop) against the CPU oracle's restatement of procimg.h's wd path,
+bit for bit: every output half, and the image modified in place by alpha over white. Cases cover the scale-1 path
+(whole 448-pixel sides, a 448 crop, vertical white pad), upscaling with white borders, downscaling from level 0 and
+from pyramid levels 1 and 2, crops, an extreme aspect ratio and padded row strides."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from tests import _gpu as G
+
+pytestmark = pytest.mark.gpu
+
+CASES = [  # w, h, alpha, rect (x0, y0, cw, ch) or None for the whole image, extra stride bytes
+    (448, 448, 0, None, 0),
+    (448, 300, 1, None, 0),
+    (897, 897, 0, (100, 200, 448, 448), 0),
+    (300, 200, 1, None, 0),
+    (1000, 700, 1, None, 64),
+    (2000, 1500, 0, None, 0),
+    (2000, 1500, 1, (100, 50, 900, 1200), 0),
+    (4000, 3000, 0, None, 16),
+    (4000, 3000, 1, (500, 300, 2400, 1800), 0),
+    (1600, 30, 0, None, 0),
+    (13, 977, 1, None, 4),
+]
+
+
+@pytest.mark.parametrize("w,h,alpha,rect,pad", CASES)
+def test_prep_matches_oracle(xlib, cuda, w, h, alpha, rect, pad):
+    import torch
+    from oracle import oracle as O
+    rng = np.random.default_rng(90 + w + h)
+    stride = 4 * w + pad
+    img = rng.integers(0, 256, (h, stride), dtype=np.uint8)
+    if alpha:  # some fully transparent and fully opaque pixels too
+        a = img[:, 3:4 * w:4]
+        a[::5, ::3] = 0
+        a[1::7, ::2] = 255
+    x0, y0, cw, ch = rect or (0, 0, w, h)
+    want_img = img.copy()
+    want = np.zeros(1024 * 592, np.uint16)
+    O.lib().or_prep(want_img, w, h, stride, alpha, x0, y0, cw, ch, want)
+    dimg = G.dev(img)
+    scratch = G.zeros((xlib.xtb_prep_scratch_bytes(w, h),), torch.uint8)
+    out = G.zeros((1024 * 592,), torch.int16)
+    out.fill_(0x5555)  # every half must be written (pad columns included)
+    assert xlib.xtb_prep_ingest(G.P(dimg), w, h, stride, alpha, G.P(scratch), None) == 0
+    assert xlib.xtb_prep_crop(G.P(dimg), w, h, stride, x0, y0, cw, ch, G.P(scratch), G.P(out), None) == 0
+    got = G.host(out).view(np.uint16)
+    gimg = G.host(dimg)
+    assert np.array_equal(gimg[:, :4 * w], want_img[:, :4 * w]), "alpha over white differs"
+    assert np.array_equal(gimg[:, 4 * w:], img[:, 4 * w:]), "bytes past the row written"
+    diff = got != want
+    assert not diff.any(), f"{int(diff.sum())} of {diff.size} halves differ (first at {np.argmax(diff)})"
+
+
+def test_prep_rejects_bad_arguments(xlib, cuda):
+    import torch
+    img = G.zeros((10, 40), torch.uint8)
+    scratch = G.zeros((xlib.xtb_prep_scratch_bytes(10, 10),), torch.uint8)
+    out = G.zeros((1024 * 592,), torch.int16)
+    assert xlib.xtb_prep_ingest(G.P(img), 10, 10, 38, 0, G.P(scratch), None) == -1      # stride < 4 w
+    assert xlib.xtb_prep_crop(G.P(img), 10, 10, 40, 5, 0, 6, 10, G.P(scratch), G.P(out), None) == -1  # rect
+    assert xlib.xtb_prep_crop(G.P(img), 10, 10, 40, 0, 0, 10, 10, None, G.P(out), None) == -1

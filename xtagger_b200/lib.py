@@ -67,6 +67,9 @@ _SIGS = {
     "xtb_oproj_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P]),
     "xtb_fc1_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P, _P, _P]),
     "xtb_fc2_sp": (C.c_int, [_P, C.c_int, _P, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
+    "xtb_prep_scratch_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "xtb_prep_ingest": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
+    "xtb_prep_crop": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P, _P]),
     "xtb_error_word": (C.c_uint32, [C.c_int]),
     "xtb_error_clear": (None, [C.c_int]),
 }
