@@ -1,0 +1,92 @@
+"""Throughput of the GPU preprocessing (xtb_prep_ingest + xtb_prep_crop: decoded RGBA image -> model input) on
+seeded synthetic images, through the C ABI. Per workload (image size, alpha) one JSON line:
+  device_img_s   images/s with the decoded images resident in HBM (a CUDA graph of `batch` images, CUDA events);
+  e2e_img_s      the same including the copy of each decoded image from pinned host memory (H2D on the stream);
+  gbs            decoded-image bytes read per second (device-resident);
+  cpu            the CPU oracle (plain C, one thread) on one image of the same size;
+  level          the pyramid level the whole-image resample reads from.
+The reference does this step on the host (src/core/procimg.h, AVX2 per worker thread); its numbers are not
+reproducible here (Windows-only build), so the oracle port stands in as the CPU baseline.
+
+    python -m xtagger_b200.bench_prep [--batch 64] [--iters 10]
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+WORKLOADS = [(1024, 1024, 1), (1600, 1200, 0), (3000, 2000, 1), (448, 448, 0)]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    sys.path.insert(0, ROOT)
+    import torch
+    from oracle import oracle as O
+    from xtagger_b200 import lib as L
+    xl = L.lib()
+    rng = np.random.default_rng(5)
+    for w, h, alpha in WORKLOADS:
+        stride = 4 * w
+        host = torch.from_numpy(rng.integers(0, 256, (a.batch, h, stride), dtype=np.uint8)).pin_memory()
+        dev = host.cuda()
+        nscr = xl.xtb_prep_scratch_bytes(w, h)
+        scratch = torch.empty((a.batch, nscr), dtype=torch.uint8, device="cuda")
+        out = torch.empty((a.batch, 1024 * 592), dtype=torch.int16, device="cuda")
+
+        def step(copy):
+            s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for i in range(a.batch):
+                if copy:
+                    dev[i].copy_(host[i], non_blocking=True)
+                p = C.c_void_p(dev[i].data_ptr())
+                assert xl.xtb_prep_ingest(p, w, h, stride, alpha, C.c_void_p(scratch[i].data_ptr()), s) == 0
+                assert xl.xtb_prep_crop(p, w, h, stride, 0, 0, w, h, C.c_void_p(scratch[i].data_ptr()),
+                                        C.c_void_p(out[i].data_ptr()), s) == 0
+
+        res = {}
+        for copy in (False, True):
+            step(copy)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream()
+            with torch.cuda.stream(st):
+                with torch.cuda.graph(g, stream=st):
+                    step(copy)
+            g.replay()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(a.iters):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1) * 1e-3)
+            res[copy] = float(np.median(ts))
+            del g
+        assert xl.xtb_error_word(0) == 0
+        img = host[0].numpy().copy()
+        o = np.zeros(1024 * 592, np.uint16)
+        t0 = time.perf_counter()
+        O.lib().or_prep(img, w, h, stride, alpha, 0, 0, w, h, o)
+        cpu = time.perf_counter() - t0
+        print(json.dumps({"workload": f"{w}x{h} RGBA{' with alpha' if alpha else ''}, whole image -> 448^2 input",
+                          "batch": a.batch, "level": O.lib().or_prep_level(w, h, max(w, h)),
+                          "device_img_s": a.batch / res[False], "e2e_img_s": a.batch / res[True],
+                          "us_per_img": res[False] / a.batch * 1e6,
+                          "gbs": a.batch * h * stride / res[False] / 1e9,
+                          "h2d_bytes_per_img": h * stride,
+                          "cpu": {"img_s": 1 / cpu, "cores": 1, "kind": "port"}}), flush=True)
+
+
+if __name__ == "__main__":
+    main()
