@@ -29,6 +29,9 @@ struct EpiQKV {
         int M;
     };
     using State = NoState;
+    // 8 KB of staging per warp on the pair GEMM: both halves of the RoPE angles (4 KB each) are brought in when the
+    // tile starts, so no angle load waits in the apply phase; the first 4 KB are reused for the output rows
+    static constexpr int STAGING_PER_WARP = 8192;
     // cq / ck / cv ride along with the block-scale promotion, so acc arrives already scaled
     __device__ __forceinline__ static float col_scale(const Params &p, const EpiCtx &cx)
     {
@@ -36,10 +39,11 @@ struct EpiQKV {
         return which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
     }
     // The RoPE angles of the warp's 32 rows (256 bytes each) are brought in through the staging buffer with
-    // coalesced loads, half a row (16 pairs) at a time: rows t of one warp are consecutive in the table, so each
-    // load instruction covers 4 whole 128-byte lines instead of 32 lines touched by one lane each.
+    // coalesced loads, half a row (16 pairs) at a time into 4 KB each: rows t of one warp are consecutive in the
+    // table, so each load instruction covers 4 whole 128-byte lines instead of 32 lines touched by one lane each.
     __device__ __forceinline__ static void stage_angles(const Params &p, const EpiCtx &cx, int h)
     {
+        uint8_t *st = cx.stage + h * 4096;
         const int t0 = cx.row0 % T;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
@@ -48,14 +52,17 @@ struct EpiQKV {
             if (tt >= T) tt -= T;
             float4 v = make_float4(1.f, 0.f, 1.f, 0.f);  // cls rows and rows past M: identity
             if (tt > 0 && cx.row0 + r < p.M) v = __ldg((const float4 *)(p.cs + (size_t)(tt - 1) * 32 + 16 * h) + c);
-            *(float4 *)stage_chunk(cx.stage, r, c) = v;
+            *(float4 *)stage_chunk(st, r, c) = v;
         }
     }
-    // The first half is staged before the accumulator is built (the staging buffer is free between tiles: the
+    // Both halves are staged before the accumulator is built (the staging buffer is free between tiles: the
     // previous tile's stores read it synchronously), so those loads overlap the main loop.
     __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &)
     {
-        if ((cx.col0 >> 10) < 2) stage_angles(p, cx, 0);
+        if ((cx.col0 >> 10) < 2) {
+            stage_angles(p, cx, 0);
+            stage_angles(p, cx, 1);
+        }
     }
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
@@ -74,18 +81,14 @@ struct EpiQKV {
                     o[hh][q] = make_uint4(w[0], w[1], w[2], w[3]);
                 }
         } else {
+            __syncwarp();
 #pragma unroll
-            for (int h = 0; h < 2; h++) {          // pairs 16 h .. 16 h + 15 (half 0 was staged by begin)
-                __syncwarp();
-                if (h == 1) {
-                    stage_angles(p, cx, 1);
-                    __syncwarp();
-                }
+            for (int h = 0; h < 2; h++) {          // pairs 16 h .. 16 h + 15 (staged by begin)
 #pragma unroll
                 for (int q2 = 0; q2 < 2; q2++) {   // 8 pairs (16 dims of each head) per step
                     float4 a[4];
 #pragma unroll
-                    for (int e = 0; e < 4; e++) a[e] = *(const float4 *)stage_chunk(cx.stage, cx.lane, 4 * q2 + e);
+                    for (int e = 0; e < 4; e++) a[e] = *(const float4 *)stage_chunk(cx.stage + h * 4096, cx.lane, 4 * q2 + e);
                     const int j = 16 * h + 8 * q2;
 #pragma unroll
                     for (int hh = 0; hh < 2; hh++) {

@@ -46,6 +46,17 @@ struct GemmCfg {
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
+// Staging bytes per epilogue warp an epilogue asks for (Epi::STAGING_PER_WARP), 4 KB by default. The CTA-pair GEMM
+// sizes its staging from it; this kernel has 4 KB per warp and accepts only epilogues that fit.
+template <class E, class = void>
+struct StagingOf {
+    static constexpr int v = 4096;
+};
+template <class E>
+struct StagingOf<E, decltype((void)E::STAGING_PER_WARP)> {
+    static constexpr int v = E::STAGING_PER_WARP;
+};
+
 // Epilogue context of one thread: output row row0 + lane, columns col0 .. col0 + COLS - 1.
 struct EpiCtx {
     int row0;        // first row of this warp's 32 rows
@@ -85,6 +96,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
            const __grid_constant__ CUtensorMap tmC, const GemmArgs g, const typename Epi::Params ep)
 {
     using C = GemmCfg<BN, EW>;
+    static_assert(StagingOf<Epi>::v <= C::STAGE_PER_WARP, "epilogue staging larger than this kernel provides");
     constexpr int STAGES = C::STAGES;
     constexpr int COLS = C::COLS;
     constexpr uint32_t IDESC = idesc_m128(BN);
@@ -212,16 +224,18 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
                 tc_fence_after();
                 const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * BN + half * COLS;
                 const float2 s2 = make_float2(s, s);
+                constexpr int CH = COLS >= 32 ? 32 : COLS;  // columns per tcgen05.wait::ld
 #pragma unroll
-                for (int c = 0; c < COLS / 16; c++) {
-                    float v[16];
-                    tmem_ld16(taddr + c * 16, v);
+                for (int c0 = 0; c0 < COLS; c0 += CH) {
+                    float v[CH];
+#pragma unroll
+                    for (int c = 0; c < CH / 16; c++) tmem_ld16(taddr + c0 + c * 16, v + 16 * c);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
+                    for (int j = 0; j < CH / 2; j++) {
                         const float2 vv = make_float2(v[2 * j], v[2 * j + 1]);
-                        if (PROMOTE) acc[c * 8 + j] = ffma2(s2, vv, acc[c * 8 + j]);
-                        else acc[c * 8 + j] = vv;
+                        if (PROMOTE) acc[c0 / 2 + j] = ffma2(s2, vv, acc[c0 / 2 + j]);
+                        else acc[c0 / 2 + j] = vv;
                     }
                 }
                 tc_fence_before();

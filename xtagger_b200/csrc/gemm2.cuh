@@ -10,6 +10,10 @@
 // single-CTA GEMM: two TMEM buffers of 256 columns, 8 epilogue warps with 128 accumulator columns per thread.
 // An MMA with N = 128 per SM would leave room for four TMEM buffers but reads shared memory faster than it can
 // supply (about 20 % below the N = 256 rate, measured both with one CTA and with pairs).
+// GROUPS (BN = 128): the four TMEM buffers go to two epilogue groups of four warps (one per lane quadrant, 128
+// columns per thread) that take the pair's tiles in turn, each promoting into its own two buffers. While one group
+// runs the fused apply phase of a tile from registers, the MMA keeps filling the other group's buffers, so the apply
+// no longer stalls the main loop (with two buffers the MMA can run at most two K blocks ahead of the epilogue).
 //
 // Roles (320 threads per CTA):
 //   warp 0      TMA producer of this CTA's A and B slices into a 6-stage ring. Completion is counted on rank 0's
@@ -25,30 +29,35 @@
 
 namespace xtb {
 
-template <int BN_>
+template <int BN_, bool GROUPS_ = false, int SPW_ = 4096>
 struct Gemm2CfgT {
     static constexpr int BN = BN_;                          // output columns per tile
+    static constexpr bool GROUPS = GROUPS_;
     static constexpr int EW = 8;                            // epilogue warps: 2 per TMEM lane quadrant
-    static constexpr int COLS = BN / 2;                     // accumulator columns per epilogue thread
+    static constexpr int COLS = GROUPS ? BN : BN / 2;       // accumulator columns per epilogue thread
+    static constexpr int TEMPTY = GROUPS ? 2 * 4 : 2 * EW;  // arrivals that free a TMEM buffer (both CTAs)
     static constexpr int A_BYTES = 128 * 128;               // this CTA's 128 A rows x one 128-byte K slice
     static constexpr int B_BYTES = (BN / 2) * 128;          // this CTA's BN / 2 B rows
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (6 * 32768) / STAGE_BYTES;  // 192 KB of ring
+    static constexpr int STAGE_PER_WARP = SPW_;             // epilogue staging per warp
+    static constexpr int STAGING = EW * SPW_;
+    static constexpr int STAGES = (7 * 32768 - STAGING) / STAGE_BYTES;  // the rest of 224 KB as ring (6 stages at 4 KB)
     static constexpr int TBUF = 512 / BN;                   // TMEM accumulator buffers
-    static constexpr int STAGING = 32768;
-    static constexpr int STAGE_PER_WARP = STAGING / EW;     // 4 KB
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + STAGING + 1024;  // + barriers
     static constexpr int THREADS = 64 + 32 * EW;
     static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(!GROUPS || BN == 128, "grouped epilogue: four 128-column buffers");
 };
 using Gemm2Cfg = Gemm2CfgT<256>;
+using Gemm2GCfg = Gemm2CfgT<128, true>;
 
-template <class Epi, bool PROMOTE, int BN = 256>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREADS, 1)
+template <class Epi, bool PROMOTE, int BN = 256, bool GROUPS = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN, GROUPS>::THREADS, 1)
     k_gemm2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             const __grid_constant__ CUtensorMap tmC, const GemmArgs g, const typename Epi::Params ep)
 {
-    using C = Gemm2CfgT<BN>;
+    using C = Gemm2CfgT<BN, GROUPS, StagingOf<Epi>::v>;
+    static_assert(!GROUPS || PROMOTE, "the grouped epilogue promotes every K block");
     constexpr int STAGES = C::STAGES, TBUF = C::TBUF, COLS = C::COLS;
     constexpr uint32_t IDESC = idesc_m256(C::BN);
     extern __shared__ uint8_t smem_raw[];
@@ -71,7 +80,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREA
         }
         for (int b = 0; b < TBUF; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 2 * C::EW);
+            mbar_init(&tempty[b], C::TEMPTY);
         }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -115,10 +124,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREA
     } else if (warp == 1) {
         if (rank == 0 && elect_one()) {
             int stage = 0;
-            uint32_t ph = 0, tb = 0, tph = 0;
+            uint32_t ph = 0, tb = 0, tph = 0, cnt[2] = {0, 0};
             bool ok = true;
-            for (int t = pair; t < total && ok; t += npairs) {
+            for (int t = pair, i = 0; t < total && ok; t += npairs, i++) {
                 for (int k = 0; k < KI; k++) {
+                    if (GROUPS) {  // group i & 1 owns buffers 2 (i & 1) and 2 (i & 1) + 1, used in turn per K block
+                        const uint32_t c = cnt[i & 1]++;
+                        tb = 2 * (i & 1) + (c & 1);
+                        tph = (c >> 1) & 1;
+                    }
                     if (PROMOTE || k == 0) {
                         if (!(ok = mbar_wait(&tempty[tb], tph ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
                         tc_fence_after();
@@ -135,7 +149,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREA
                     umma_commit_pair(&empty[stage], 0x3);
                     if (PROMOTE || k == KI - 1) {
                         umma_commit_pair(&tfull[tb], 0x3);
-                        if (++tb == TBUF) {
+                        if (!GROUPS && ++tb == TBUF) {
                             tb = 0;
                             tph ^= 1;
                         }
@@ -150,18 +164,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREA
     } else {
         const int ew = warp - 2;
         const int quad = warp & 3;
-        const int half = ew >> 2;  // which COLS-wide half of the tile
+        const int half = ew >> 2;  // which COLS-wide half of the tile (GROUPS: which epilogue group)
         const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
         EpiCtx cx;
         cx.lane = lane;
         cx.stage = sStage + ew * C::STAGE_PER_WARP;
         cx.tmC = &tmC;
-        uint32_t tb = 0, tph = 0;
+        uint32_t tb = 0, tph = 0, c = 0;
         bool ok = true;
-        for (int t = pair; t < total && ok; t += npairs) {
+        for (int t = pair + (GROUPS ? half * npairs : 0); t < total && ok; t += (GROUPS ? 2 : 1) * npairs) {
             const int nb = t % g.n_tiles, mb = t / g.n_tiles;
             cx.row0 = mb * 256 + rank * 128 + quad * 32;
-            cx.col0 = nb * C::BN + half * COLS;
+            cx.col0 = nb * C::BN + (GROUPS ? 0 : half * COLS);
             typename Epi::State es;
             Epi::begin(ep, cx, es);  // per-tile loads issued before the accumulator is ready
             float2 acc[COLS / 2];
@@ -175,10 +189,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREA
             for (int u = 0; u < units; u++) {
                 const float s = PROMOTE ? amul * snext : 1.0f;
                 if (PROMOTE && u + 1 < units) snext = __ldg(wsr + u + 1);
+                if (GROUPS) {
+                    tb = 2 * half + (c & 1);
+                    tph = (c >> 1) & 1;
+                    c++;
+                }
                 // warp-uniform outcome: the tcgen05.ld below is a .sync.aligned warp instruction
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
                 tc_fence_after();
-                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * C::BN + half * COLS;
+                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * C::BN + (GROUPS ? 0 : half * COLS);
                 const float2 s2 = make_float2(s, s);
                 constexpr int CH = COLS <= 64 ? COLS : 32;  // columns per tcgen05.wait::ld
 #pragma unroll
@@ -199,7 +218,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN>::THREA
                         else acc[c0 / 2 + j] = vv;
                     }
                 }
-                if (++tb == TBUF) {
+                if (!GROUPS && ++tb == TBUF) {
                     tb = 0;
                     tph ^= 1;
                 }

@@ -78,13 +78,13 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
 
 // One launch of the CTA-pair GEMM (block-scaled E4M3): 256 x 128 tiles, one cluster of two CTAs per tile at a
 // time, as many clusters as can be resident (a persistent grid).
-template <class Epi>
+template <class Epi, int BN = 256, bool GROUPS = false>
 static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
                      const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
                      uint32_t *err = nullptr)
 {
-    using Cfg = Gemm2Cfg;
-    auto kern = k_gemm2<Epi, true>;
+    using Cfg = Gemm2CfgT<BN, GROUPS, StagingOf<Epi>::v>;
+    auto kern = k_gemm2<Epi, true, BN, GROUPS>;
     if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
     if (a.row_bytes != b.row_bytes || M <= 0 || N <= 0 || a.box_rows != A_BOX_ROWS || b.box_rows != Cfg::BN / 2) {
         fprintf(stderr, "eva: pair gemm operands (K bytes %d vs %d, boxes %d / %d rows, M %d, N %d)\n", a.row_bytes,
@@ -120,26 +120,45 @@ static int kb(int k) { return (k + 127) / 128; }
 #ifndef XTB_PAIR_MASK
 #define XTB_PAIR_MASK 0x9  // bit u set: WeightUse u on the CTA-pair GEMM (QKV, fc2)
 #endif
-static constexpr bool kPair[5] = {(XTB_PAIR_MASK & 1) != 0, (XTB_PAIR_MASK & 2) != 0, (XTB_PAIR_MASK & 4) != 0,
-                                  (XTB_PAIR_MASK & 8) != 0, (XTB_PAIR_MASK & 16) != 0};
+// bit u set: WeightUse u on the CTA-pair GEMM with N = 128 and two epilogue groups (takes precedence)
+#ifndef XTB_PAIRG_MASK
+#define XTB_PAIRG_MASK 0x0
+#endif
+static constexpr bool kPairG[5] = {(XTB_PAIRG_MASK & 1) != 0, (XTB_PAIRG_MASK & 2) != 0, (XTB_PAIRG_MASK & 4) != 0,
+                                   (XTB_PAIRG_MASK & 8) != 0, (XTB_PAIRG_MASK & 16) != 0};
+static constexpr bool kPair[5] = {(XTB_PAIR_MASK & 1) != 0 && !kPairG[0], (XTB_PAIR_MASK & 2) != 0 && !kPairG[1],
+                                  (XTB_PAIR_MASK & 4) != 0 && !kPairG[2], (XTB_PAIR_MASK & 8) != 0 && !kPairG[3],
+                                  (XTB_PAIR_MASK & 16) != 0 && !kPairG[4]};
 
-int weight_box_rows(WeightUse u) { return kPair[u] ? Gemm2Cfg::BN / 2 : 256; }
+int weight_box_rows(WeightUse u) { return kPairG[u] ? Gemm2GCfg::BN / 2 : kPair[u] ? Gemm2Cfg::BN / 2 : 256; }
 
 template <class Epi, WeightUse U>
 static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep, cudaStream_t st,
                     const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
 {
-    if constexpr (kPair[U])
+    if constexpr (kPairG[U])
+        return run_gemm2<Epi, 128, true>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
+    else if constexpr (kPair[U])
         return run_gemm2<Epi>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else
         return run_gemm<Epi, 256, false, true, false>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
 }
 
+// Opt the projection kernel of (Epi, U) into its shared memory and check that its clusters fit (pair kernels).
 template <class Epi, WeightUse U>
-static const void *proj_kernel()
+static int prepare_proj()
 {
-    if constexpr (kPair[U]) return (const void *)k_gemm2<Epi, true>;
-    else return (const void *)k_gemm<Epi, 256, false, true, false>;
+    if constexpr (kPairG[U]) {
+        using Cfg = Gemm2CfgT<128, true, StagingOf<Epi>::v>;
+        const void *k = (const void *)k_gemm2<Epi, true, 128, true>;
+        return set_smem(k, Cfg::SMEM) || max_pairs(k, Cfg::THREADS, Cfg::SMEM) <= 0 ? -1 : 0;
+    } else if constexpr (kPair[U]) {
+        using Cfg = Gemm2CfgT<256, false, StagingOf<Epi>::v>;
+        const void *k = (const void *)k_gemm2<Epi, true>;
+        return set_smem(k, Cfg::SMEM) || max_pairs(k, Cfg::THREADS, Cfg::SMEM) <= 0 ? -1 : 0;
+    } else {
+        return set_smem((const void *)k_gemm<Epi, 256, false, true, false>, GemmCfg<256>::SMEM);
+    }
 }
 
 int launch_gemm_f32(const Operand &a, const Weight8 &w, float ascale, float *out, int ldo, cudaStream_t st)
@@ -367,19 +386,9 @@ int prepare_kernels()
     const void *single[] = {(const void *)k_gemm<EpiPatch, 256, true, false, false>};
     for (const void *k : single)
         if (set_smem(k, GemmCfg<256>::SMEM)) return -1;
-    const void *proj[5];  // indexed by WeightUse
-    proj[W_QKV] = proj_kernel<EpiQKV, W_QKV>();
-    proj[W_O] = proj_kernel<EpiResid, W_O>();
-    proj[W_FC1] = proj_kernel<EpiFC1, W_FC1>();
-    proj[W_FC2] = proj_kernel<EpiFC2, W_FC2>();
-    proj[W_F32] = proj_kernel<EpiF32<128>, W_F32>();
-    for (int u = 0; u < 5; u++) {
-        if (!kPair[u]) {
-            if (set_smem(proj[u], GemmCfg<256>::SMEM)) return -1;
-        } else if (set_smem(proj[u], Gemm2Cfg::SMEM) || max_pairs(proj[u], Gemm2Cfg::THREADS, Gemm2Cfg::SMEM) <= 0) {
-            return -1;
-        }
-    }
+    if (prepare_proj<EpiQKV, W_QKV>() || prepare_proj<EpiResid, W_O>() || prepare_proj<EpiFC1, W_FC1>() ||
+        prepare_proj<EpiFC2, W_FC2>() || prepare_proj<EpiF32<128>, W_F32>())
+        return -1;
     const void *g64[] = {(const void *)k_gemm<EpiHead<32>, 64, true, false, false>,
                          (const void *)k_gemm<EpiHead<32>, 64, false, true, true>};
     for (const void *k : g64)
