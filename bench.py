@@ -295,6 +295,7 @@ def main():
         args.batch = 128 if args.sparse else 64
     if args.sparse:
         MODEL_KW["prune24"] = True
+        os.environ.setdefault("XTB_SPARSE", "1")  # the engine's sparse kernels are opt-in
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:

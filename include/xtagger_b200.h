@@ -94,8 +94,9 @@ int eva_download(eva *e, float *out, uint32_t n);
 void *eva_stream(eva *e, int i);
 /* Number of kernel launches in one forward on one device. */
 int eva_launches_per_forward(eva *e);
-/* Projection kinds running on the 2:4-sparse tensor-core kernels (bit 0 QKV, 1 O, 2 W12, 3 W2): the kinds whose
- * weights are 2:4 along k in every layer (as prune24.py writes them), unless XTB_SPARSE=0 was set at open. */
+/* Projection kinds running on the 2:4-sparse tensor-core kernels (bit 0 QKV, 1 O, 2 W12, 3 W2): with XTB_SPARSE=1 in
+ * the environment at open, the kinds whose weights are 2:4 along k in every layer (as prune24.py writes them);
+ * otherwise 0 (the dense kernels are faster on the same weights). */
 int eva_sparse_kinds(eva *e);
 /* One direct (non-graph) forward on device 0 with an event after every kernel; per-kernel-kind milliseconds into
  * ms[kinds] (names from eva_prof_name), returns the number of kinds or -1. Mirrors the reference's EVA_PROF

@@ -50,12 +50,17 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     alt = O.forward(models[name], x, key_tile=128, slice_rows=1)   # another tiling of the same arithmetic
     floor_max = float(np.abs(alt - want).max())
     floor_mean = float(np.abs(alt - want).mean())
-    eng = Engine(models[name], nb=max(nimg, 2))
+    if name.endswith("_p"):
+        os.environ["XTB_SPARSE"] = "1"  # pruned models: the sparse kernels (opt-in)
     try:
-        got = eng.run(x)
-        assert eng.sparse_kinds() == (15 if name.endswith("_p") else 0)
+        eng = Engine(models[name], nb=max(nimg, 2))
+        try:
+            got = eng.run(x)
+            assert eng.sparse_kinds() == (15 if name.endswith("_p") else 0)
+        finally:
+            eng.close()
     finally:
-        eng.close()
+        os.environ.pop("XTB_SPARSE", None)
     assert xlib.xtb_error_word(0) == 0
     assert np.isfinite(got).all()
     err = np.abs(got - want)

@@ -8,9 +8,11 @@
 // scores (and head inputs), event; eva_wait sleeps on the events. Multi-GPU: one replica per device with its own
 // stream and graph; a submit's inputs are split into contiguous shards, one per device, and the scores land in
 // disjoint rows of one host slot. No collective is involved.
-// 2:4-sparse weights (prune24.py's output, or a block-scaled file pruned the same way): every projection kind whose
-// weights are 2:4 along k in all layers is compressed at bring-up and runs on the sparse tensor cores
-// (tcgen05.mma.sp, gemm_sp.cuh) with the same results; XTB_SPARSE=0 in the environment keeps the dense kernels.
+// 2:4-sparse weights (prune24.py's output, or a block-scaled file pruned the same way): with XTB_SPARSE=1 in the
+// environment, every projection kind whose weights are 2:4 along k in all layers is compressed at bring-up and runs
+// on the sparse tensor cores (tcgen05.mma.sp, gemm_sp.cuh) with the same results. Off by default: on B200 the
+// transposed epilogues the sparse operand forces cost more than the sparse MMA saves, so the dense kernels are
+// faster on the same pruned weights.
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -323,7 +325,7 @@ int sparse_prepare(Impl *im, Replica &r, const uint8_t *hostblob)
 {
     im->sp_ready = true;
     const char *env = getenv("XTB_SPARSE");
-    if (env && env[0] == '0') return 0;
+    if (!env || env[0] != '1') return 0;
     auto host_w = [&](int i, int g) { return hostblob + ((const uint8_t *)r.L[i].w[g].op.ptr - r.wts); };
     for (int g = 0; g < NG; g++) {
         bool all = true;
