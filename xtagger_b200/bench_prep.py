@@ -8,7 +8,7 @@ seeded synthetic images, through the C ABI. Per workload (image size, alpha) one
 The reference does this step on the host (src/core/procimg.h, AVX2 per worker thread); its numbers are not
 reproducible here (Windows-only build), so the oracle port stands in as the CPU baseline.
 
-    python -m xtagger_b200.bench_prep [--batch 64] [--iters 10]
+    python -m xtagger_b200.bench_prep [--batch 64] [--iters 10] [--sizes 0,1,2,3]
 """
 import argparse
 import ctypes as C
@@ -27,6 +27,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--sizes", default="", help="indices into the workload list (default: all)")
     a = ap.parse_args()
     sys.path.insert(0, ROOT)
     import torch
@@ -34,7 +35,8 @@ def main():
     from xtagger_b200 import lib as L
     xl = L.lib()
     rng = np.random.default_rng(5)
-    for w, h, alpha in WORKLOADS:
+    pick = [int(i) for i in a.sizes.split(",") if i] or range(len(WORKLOADS))
+    for w, h, alpha in (WORKLOADS[i] for i in pick):
         stride = 4 * w
         host = torch.from_numpy(rng.integers(0, 256, (a.batch, h, stride), dtype=np.uint8)).pin_memory()
         dev = host.cuda()
