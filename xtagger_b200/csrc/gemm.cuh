@@ -35,7 +35,7 @@ struct GemmCfg {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int STAGES = (6 * 32768) / STAGE_BYTES;  // 192 KB of ring: 4 stages at BN 256 / 192, 6 at 128
     static constexpr int EPI_WARPS = EW;   // epilogue warps: EW / 4 per TMEM lane quadrant
     static constexpr int COLS = BN / (EW / 4);  // accumulator columns per epilogue thread
     static constexpr int TBUF = 512 / BN;  // TMEM accumulator buffers (512 columns in all)
