@@ -4,6 +4,9 @@ E4M3 weights (24 layers, 10861 tags, FP8 head).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 64] [--nt 10861] [--sparse]
 
+--v3 runs the same forward on weights in the reference's own eva02.bin v3 format (one E4M3 scale per tensor, fp16
+head): the GEMMs then accumulate the whole K range in TMEM and scale once, as the reference's kernels do. This is
+the format oracle/ref_time.py times the reference's kernels on.
 --sparse is config 5: the four projections of every layer 2:4-pruned by magnitude (prune24.py's rule), which the
 engine runs on the sparse tensor cores (tcgen05.mma.sp); global batch 128 unless --batch is given.
 
@@ -237,9 +240,10 @@ def run_ours(args, rank, world, local):
                 "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
                 "config": {"workload": f"{config_name(args)}: EVA02-L 448^2 forward (24 layers, d 1024, 1025 tokens, {args.nt}-tag "
-                                       "FP8 head), global batch split across the GPUs",
+                                       f"{'fp16' if args.v3 else 'FP8'} head), global batch split across the GPUs",
                            "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
-                           "weights": "random-init, E4M3 with fp32 scales per 128x128 block" +
+                           "weights": ("random-init, E4M3 with one fp32 scale per tensor (eva02.bin v3), fp16 head"
+                                       if args.v3 else "random-init, E4M3 with fp32 scales per 128x128 block") +
                                       (", QKV / O / W12 / W2 2:4-pruned by magnitude" if args.sparse else ""),
                            "sparse_kinds": sparse_kinds,
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
@@ -269,6 +273,8 @@ def config_name(args):
     5: 2:4-sparse projections)."""
     if args.sparse:
         return "config 5"
+    if args.v3:
+        return f"batch {args.batch}, {args.nt} tags, reference v3 weights"
     if args.nt == NT and args.batch == 1:
         return "config 2"
     if args.nt == NT and args.batch == 64:
@@ -288,11 +294,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
     ap.add_argument("--sparse", action="store_true", help="config 5: 2:4-pruned projections on the sparse kernels")
+    ap.add_argument("--v3", action="store_true", help="weights in the reference's v3 format (per-tensor scales)")
     args = ap.parse_args()
     rank, world, local = dist_env()
     MODEL_KW["nt"] = args.nt
     if args.batch is None:
         args.batch = 128 if args.sparse else 64
+    if args.v3:
+        MODEL_KW.update(version=3, head_fp8=False)
     if args.sparse:
         MODEL_KW["prune24"] = True
         os.environ.setdefault("XTB_SPARSE", "1")  # the engine's sparse kernels are opt-in

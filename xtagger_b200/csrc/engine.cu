@@ -224,6 +224,7 @@ int layout(Impl *im, Replica &r, const uint8_t *hostblob)
                 so += cnt;
             }
             L.w[g].ws = sp[g];
+            L.w[g].uniform = v4 ? 0.0f : tb[g];  // v3: one scale per tensor, applied once after the K sum
             L.w[g].n = n;
             L.w[g].k = k;
             RCK(make_operand(&L.w[g].op, wp[g], n, k, weight_box_rows((WeightUse)g)));  // g: W_QKV, W_O, W_FC1, W_FC2

@@ -13,8 +13,9 @@
 // own TMEM buffer (two buffers of BN columns, ping-pong), and the epilogue warps fold it into fp32 registers with
 // acc += (a_scale * w_scale[block]) * partial (packed fma.rn.f32x2). This keeps the dequantize-then-matmul
 // semantics exactly (scales are arbitrary fp32, not powers of two) while the tensor core runs the next K block into
-// the other buffer. Without PROMOTE the whole K range accumulates in one TMEM buffer; the buffers ping-pong across
-// tiles so that the epilogue of one tile overlaps the main loop of the next.
+// the other buffer. Without PROMOTE the whole K range accumulates in one TMEM buffer and is scaled once by
+// a_scale * wsu (a weight with one scale for the whole tensor, as the reference's v3 format, or 1 for fp16); the
+// buffers ping-pong across tiles so that the epilogue of one tile overlaps the main loop of the next.
 #pragma once
 #include "ptx.cuh"
 
@@ -26,7 +27,8 @@ struct GemmArgs {
     int m_tiles, n_tiles;
     const float *ws;     // PROMOTE: block scales [ws_rows][ws_ld]; row = N block (or M block when WS_ON_M)
     int ws_ld, ws_rows;
-    float ascale;        // activation dequant scale, folded into every block scale (PROMOTE only)
+    float ascale;        // activation dequant scale, folded into every block scale (or into wsu)
+    float wsu;           // without PROMOTE: the one weight scale of the tensor (1 for unscaled fp16 operands)
     uint32_t *err;       // library error word
 };
 
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
             float snext = PROMOTE ? __ldg(wsr) : 1.0f;
             const float amul = g.ascale * Epi::col_scale(ep, cx);  // activation dequant x the epilogue's own factor
             for (int u = 0; u < units; u++) {
-                const float s = PROMOTE ? amul * snext : 1.0f;
+                const float s = PROMOTE ? amul * snext : amul * g.wsu;
                 if (PROMOTE && u + 1 < units) snext = __ldg(wsr + u + 1);
                 // warp-uniform outcome: the tcgen05.ld below is a .sync.aligned warp instruction
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
@@ -235,7 +237,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
                     for (int j = 0; j < CH / 2; j++) {
                         const float2 vv = make_float2(v[2 * j], v[2 * j + 1]);
                         if (PROMOTE) acc[c0 / 2 + j] = ffma2(s2, vv, acc[c0 / 2 + j]);
-                        else acc[c0 / 2 + j] = vv;
+                        else acc[c0 / 2 + j] = mul2(s2, vv);
                     }
                 }
                 tc_fence_before();

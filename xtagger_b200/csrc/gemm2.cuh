@@ -187,7 +187,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN, GROUPS
             float snext = PROMOTE ? __ldg(wsr) : 1.0f;
             const float amul = g.ascale * Epi::col_scale(ep, cx);
             for (int u = 0; u < units; u++) {
-                const float s = PROMOTE ? amul * snext : 1.0f;
+                const float s = PROMOTE ? amul * snext : amul * g.wsu;
                 if (PROMOTE && u + 1 < units) snext = __ldg(wsr + u + 1);
                 if (GROUPS) {
                     tb = 2 * half + (c & 1);
@@ -215,7 +215,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN, GROUPS
                     for (int j = 0; j < CH / 2; j++) {
                         const float2 vv = make_float2(v[2 * j], v[2 * j + 1]);
                         if (PROMOTE) acc[c0 / 2 + j] = ffma2(s2, vv, acc[c0 / 2 + j]);
-                        else acc[c0 / 2 + j] = vv;
+                        else acc[c0 / 2 + j] = mul2(s2, vv);
                     }
                 }
                 if (!GROUPS && ++tb == TBUF) {

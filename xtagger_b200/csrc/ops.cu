@@ -46,7 +46,7 @@ static int set_smem(const void *kern, size_t bytes)
 template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
 static int run_gemm(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
                     const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
-                    uint32_t *err = nullptr)
+                    uint32_t *err = nullptr, float wsu = 1.0f)
 {
     using Cfg = GemmCfg<BN>;
     auto kern = k_gemm<Epi, BN, F16, PROMOTE, WS_ON_M>;
@@ -67,6 +67,7 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     g.ws_ld = ws_ld;
     g.ws_rows = ws_rows;
     g.ascale = ascale;
+    g.wsu = wsu;
     g.err = err ? err : error_word(dev);
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
@@ -78,13 +79,13 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
 
 // One launch of the CTA-pair GEMM (block-scaled E4M3): 256 x 128 tiles, one cluster of two CTAs per tile at a
 // time, as many clusters as can be resident (a persistent grid).
-template <class Epi, int BN = 256, bool GROUPS = false>
+template <class Epi, int BN = 256, bool GROUPS = false, bool PROMOTE = true>
 static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
                      const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
-                     uint32_t *err = nullptr)
+                     uint32_t *err = nullptr, float wsu = 1.0f)
 {
     using Cfg = Gemm2CfgT<BN, GROUPS, StagingOf<Epi>::v>;
-    auto kern = k_gemm2<Epi, true, BN, GROUPS>;
+    auto kern = k_gemm2<Epi, PROMOTE, BN, GROUPS>;
     if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
     if (a.row_bytes != b.row_bytes || M <= 0 || N <= 0 || a.box_rows != A_BOX_ROWS || b.box_rows != Cfg::BN / 2) {
         fprintf(stderr, "eva: pair gemm operands (K bytes %d vs %d, boxes %d / %d rows, M %d, N %d)\n", a.row_bytes,
@@ -102,6 +103,7 @@ static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const flo
     g.ws_ld = ws_ld;
     g.ws_rows = ws_rows;
     g.ascale = ascale;
+    g.wsu = wsu;
     g.err = err ? err : error_word(dev);
     const int total = g.m_tiles * g.n_tiles;
     int pairs = max_pairs((const void *)kern, Cfg::THREADS, Cfg::SMEM);
@@ -136,6 +138,13 @@ template <class Epi, WeightUse U>
 static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep, cudaStream_t st,
                     const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
 {
+    if (!kPairG[U] && w.uniform > 0.0f) {  // one scale for the whole weight: accumulate over K in TMEM, scale once
+        if constexpr (kPair[U])
+            return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
+        else
+            return run_gemm<Epi, 256, false, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err,
+                                                           w.uniform);
+    }
     if constexpr (kPairG[U])
         return run_gemm2<Epi, 128, true>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else if constexpr (kPair[U])
@@ -154,10 +163,16 @@ static int prepare_proj()
         return set_smem(k, Cfg::SMEM) || max_pairs(k, Cfg::THREADS, Cfg::SMEM) <= 0 ? -1 : 0;
     } else if constexpr (kPair[U]) {
         using Cfg = Gemm2CfgT<256, false, StagingOf<Epi>::v>;
-        const void *k = (const void *)k_gemm2<Epi, true>;
-        return set_smem(k, Cfg::SMEM) || max_pairs(k, Cfg::THREADS, Cfg::SMEM) <= 0 ? -1 : 0;
+        const void *k = (const void *)k_gemm2<Epi, true>, *ku = (const void *)k_gemm2<Epi, false>;
+        return set_smem(k, Cfg::SMEM) || max_pairs(k, Cfg::THREADS, Cfg::SMEM) <= 0 || set_smem(ku, Cfg::SMEM) ||
+                       max_pairs(ku, Cfg::THREADS, Cfg::SMEM) <= 0
+                   ? -1
+                   : 0;
     } else {
-        return set_smem((const void *)k_gemm<Epi, 256, false, true, false>, GemmCfg<256>::SMEM);
+        return set_smem((const void *)k_gemm<Epi, 256, false, true, false>, GemmCfg<256>::SMEM) ||
+                       set_smem((const void *)k_gemm<Epi, 256, false, false, false>, GemmCfg<256>::SMEM)
+                   ? -1
+                   : 0;
     }
 }
 

@@ -31,11 +31,14 @@ int make_operand(Operand *op, const void *ptr, int rows, int row_bytes, int box_
 enum WeightUse { W_QKV = 0, W_O = 1, W_FC1 = 2, W_FC2 = 3, W_F32 = 4 };
 int weight_box_rows(WeightUse u);
 
-// Block-scaled weight: E4M3 [n][k] plus fp32 scales [ceil(n / 128)][ceil(k / 128)].
+// Block-scaled weight: E4M3 [n][k] plus fp32 scales [ceil(n / 128)][ceil(k / 128)]. uniform > 0: every block scale
+// equals it (the reference's per-tensor v3 weights): the GEMM accumulates the whole K range in TMEM and scales
+// once, as the reference's kernels do (alpha = w_dq a_dq after the fp32 sum), instead of promoting every K block.
 struct Weight8 {
     Operand op;
     const float *ws;
     int n, k;
+    float uniform = 0.0f;
 };
 
 struct Attn {
