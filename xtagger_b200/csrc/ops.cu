@@ -190,7 +190,16 @@ int launch_patch_embed(const Operand &in, const Operand &pe, int nimg, const flo
 
 int launch_ln_e4m3(const __half *x, const float *g, const float *b, uint8_t *y, int rows, float qs, cudaStream_t st)
 {
-    k_ln_e4m3<<<(rows + 7) / 8, 256, 0, st>>>(x, g, b, y, rows, qs);
+    if (set_smem((const void *)k_ln_e4m3, LN_SMEM)) return -1;
+    if (((uintptr_t)x & 15) || rows <= 0) {
+        fprintf(stderr, "eva: layernorm input %p not 16-byte aligned or %d rows\n", (const void *)x, rows);
+        return -1;
+    }
+    const int dev = current_device();
+    int grid = LN_BLOCKS_PER_SM * num_sms(dev);
+    const int need = (rows + LN_WARPS - 1) / LN_WARPS;
+    if (grid > need) grid = need;
+    k_ln_e4m3<<<grid, LN_WARPS * 32, LN_SMEM, st>>>(x, g, b, y, rows, qs, error_word(dev));
     XTB_CK(cudaGetLastError());
     return 0;
 }
@@ -413,6 +422,7 @@ int prepare_kernels()
                         (const void *)k_gemm_sp<SpFC1>};
     for (const void *k : sp)
         if (set_smem(k, SpCfg::SMEM)) return -1;
+    if (set_smem((const void *)k_ln_e4m3, LN_SMEM)) return -1;
     return set_smem((const void *)k_attention, ATT_SMEM);
 }
 

@@ -116,6 +116,16 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *m, const vo
                  "r"(smem_u32(src)), "r"(x), "r"(y)
                  : "memory");
 }
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16), completion counted in
+// bytes on the mbarrier.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // the shared-memory sources of every committed group have been read (the buffer may be rewritten)
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

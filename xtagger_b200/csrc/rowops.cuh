@@ -7,55 +7,87 @@
 namespace xtb {
 
 // LayerNorm over 1024 fp16 values (eps 1e-6, two-pass mean / variance from registers), * gamma + beta, * qs,
-// E4M3 with saturation. One warp per row, 8 rows per 256-thread block; 16-byte loads, 8-byte stores.
-// Replaces k_ln / ln_row<1> (kern_common.cuh:147-186).
-__global__ void __launch_bounds__(256) k_ln_e4m3(const __half *__restrict__ x, const float *__restrict__ g,
-                                                 const float *__restrict__ bta, uint8_t *__restrict__ y, int rows,
-                                                 float qs)
+// E4M3 with saturation. Replaces k_ln / ln_row<1> (kern_common.cuh:147-186), same arithmetic in the same order.
+// Persistent warps: warp w of the grid takes rows w, w + W, ... and keeps LN_DEPTH of them in flight as 2 KB bulk
+// copies (cp.async.bulk, completion on one mbarrier per slot) into its own shared-memory ring, so the HBM latency is
+// covered by copies instead of by registers; gamma and beta of the lane's 32 columns stay in registers for all of
+// the warp's rows. A lane reads the 16-byte chunks lane + 32 i of a row (conflict-free) and writes 8 bytes each.
+constexpr int LN_WARPS = 8, LN_DEPTH = 4, LN_BLOCKS_PER_SM = 2;
+constexpr int LN_SMEM = LN_WARPS * LN_DEPTH * D * 2 + LN_WARPS * LN_DEPTH * 8;
+
+__global__ void __launch_bounds__(LN_WARPS * 32, LN_BLOCKS_PER_SM)
+    k_ln_e4m3(const __half *__restrict__ x, const float *__restrict__ g, const float *__restrict__ bta,
+              uint8_t *__restrict__ y, int rows, float qs, uint32_t *err)
 {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const uint4 *xr = (const uint4 *)(x + (size_t)row * D);
-    float v[32];
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint4 u = xr[lane + 32 * i];
-        const __half2 *hp = (const __half2 *)&u;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const float2 f = __half22float2(hp[e]);
-            v[8 * i + 2 * e] = f.x;
-            v[8 * i + 2 * e + 1] = f.y;
-            s += f.x + f.y;
+    extern __shared__ __align__(128) uint8_t ln_smem[];
+    const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t *ring = ln_smem + wl * LN_DEPTH * D * 2;
+    uint64_t *bar = (uint64_t *)(ln_smem + LN_WARPS * LN_DEPTH * D * 2) + wl * LN_DEPTH;
+    const int W = gridDim.x * LN_WARPS;
+    const int w0 = blockIdx.x * LN_WARPS + wl;
+    if (lane == 0) {
+        for (int s = 0; s < LN_DEPTH; s++) mbar_init(&bar[s], 1);
+        fence_mbar_init();
+        for (int s = 0; s < LN_DEPTH; s++) {
+            const int r = w0 + s * W;
+            if (r < rows) {
+                mbar_arrive_expect_tx(&bar[s], D * 2);
+                bulk_load(ring + s * D * 2, x + (size_t)r * D, D * 2, &bar[s]);
+            }
         }
     }
-    const float mean = warp_sum(s) * (1.0f / D);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        const float dx = v[i] - mean;
-        q += dx * dx;
-    }
-    const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
-    uint2 *yr = (uint2 *)(y + (size_t)row * D);
+    __syncwarp();
+    float gv[32], bv[32];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int c = 8 * (lane + 32 * i);
-        const float4 g0 = *(const float4 *)(g + c), g1 = *(const float4 *)(g + c + 4);
-        const float4 b0 = *(const float4 *)(bta + c), b1 = *(const float4 *)(bta + c + 4);
-        const float *w = v + 8 * i;
-        float o[8];
-        o[0] = (w[0] - mean) * rstd * g0.x + b0.x;
-        o[1] = (w[1] - mean) * rstd * g0.y + b0.y;
-        o[2] = (w[2] - mean) * rstd * g0.z + b0.z;
-        o[3] = (w[3] - mean) * rstd * g0.w + b0.w;
-        o[4] = (w[4] - mean) * rstd * g1.x + b1.x;
-        o[5] = (w[5] - mean) * rstd * g1.y + b1.y;
-        o[6] = (w[6] - mean) * rstd * g1.z + b1.z;
-        o[7] = (w[7] - mean) * rstd * g1.w + b1.w;
-        yr[lane + 32 * i] = make_uint2(e4m3x2(o[0] * qs, o[1] * qs) | (e4m3x2(o[2] * qs, o[3] * qs) << 16),
-                                       e4m3x2(o[4] * qs, o[5] * qs) | (e4m3x2(o[6] * qs, o[7] * qs) << 16));
+        *(float4 *)(gv + 8 * i) = __ldg((const float4 *)(g + c));
+        *(float4 *)(gv + 8 * i + 4) = __ldg((const float4 *)(g + c + 4));
+        *(float4 *)(bv + 8 * i) = __ldg((const float4 *)(bta + c));
+        *(float4 *)(bv + 8 * i + 4) = __ldg((const float4 *)(bta + c + 4));
+    }
+    for (int k = 0, row = w0; row < rows; k++, row += W) {
+        const int s = k % LN_DEPTH;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (k / LN_DEPTH) & 1, err, XTB_ERR_WAIT_TMA))) return;
+        const uint4 *xr = (const uint4 *)(ring + s * D * 2);
+        float v[32];
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint4 u = xr[lane + 32 * i];
+            const __half2 *hp = (const __half2 *)&u;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(hp[e]);
+                v[8 * i + 2 * e] = f.x;
+                v[8 * i + 2 * e + 1] = f.y;
+                sum += f.x + f.y;
+            }
+        }
+        // every lane has its row in registers: the slot goes back to the copy engine for row + LN_DEPTH * W
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row + LN_DEPTH * W < rows) {
+            mbar_arrive_expect_tx(&bar[s], D * 2);
+            bulk_load(ring + s * D * 2, x + (size_t)(row + LN_DEPTH * W) * D, D * 2, &bar[s]);
+        }
+        const float mean = warp_sum(sum) * (1.0f / D);
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const float dx = v[i] - mean;
+            q += dx * dx;
+        }
+        const float rstd = rsqrtf(warp_sum(q) * (1.0f / D) + 1e-6f);
+        uint2 *yr = (uint2 *)(y + (size_t)row * D);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = (v[8 * i + e] - mean) * rstd * gv[8 * i + e] + bv[8 * i + e];
+            yr[lane + 32 * i] = make_uint2(e4m3x2(o[0] * qs, o[1] * qs) | (e4m3x2(o[2] * qs, o[3] * qs) << 16),
+                                           e4m3x2(o[4] * qs, o[5] * qs) | (e4m3x2(o[6] * qs, o[7] * qs) << 16));
+        }
     }
 }
 
