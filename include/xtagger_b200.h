@@ -155,6 +155,11 @@ int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *p
 int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x,
                     const float *stat, const float *c, const float *d, void *stream);
 
+/* Calibration statistic (the reference's k_amax, kern_common.cuh:194-217): amax[c] = max(amax[c], max over rows of
+ * |x[row][c]|) for an fp16 [rows][k] tensor (k a multiple of 8, 16-byte aligned); amax holds non-negative fp32 values
+ * (start from zeros). Used by the calibration forward (xtagger_b200/calib.py). */
+int xtb_amax_f16(const uint16_t *x, int k, int rows, float *amax, void *stream);
+
 /* ---- 2:4-sparse weights on the sparse tensor cores (tcgen05.mma.sp) ----
  * The reference prunes weights 2:4 offline (prune24.py:44-56: in every group of four consecutive k the two least
  * important bytes are zeroed) and runs them through its dense kernels. These entry points run such weights on the

@@ -130,6 +130,11 @@ int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *p
     return launch_head_e4m3(W, B, ascale, nimg, nt, hb, out, S(stream));
 }
 
+int xtb_amax_f16(const uint16_t *x, int k, int rows, float *amax, void *stream)
+{
+    return launch_amax_f16((const __half *)x, k, rows, amax, S(stream));
+}
+
 // ---- 2:4-sparse weights ----
 int xtb_sparse24_check(const uint8_t *w, int n, int k) { return sparse24_check(w, n, k); }
 

@@ -375,6 +375,17 @@ int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, _
     return run_gemm_sp<SpResid<true>>(w, h8, rows, ascale, p, st, &xm);
 }
 
+int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t st)
+{
+    if (K <= 0 || (K & 7) || rows <= 0 || ((uintptr_t)x & 15)) {
+        fprintf(stderr, "eva: amax: bad shape %d x %d (K a multiple of 8, 16-byte aligned rows)\n", rows, K);
+        return -1;
+    }
+    k_amax<<<dim3((K / 8 + 127) / 128, std::min(rows, 64)), 128, 0, st>>>(x, K, rows, (unsigned *)amax);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
                    float qs_head, cudaStream_t st)
 {

@@ -99,6 +99,9 @@ int launch_fc1_sp(const Operand &h, const SparseW &w, float ascale, int rows, ui
 int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
                   const float *d, cudaStream_t st);
 
+// Per-column max |x| of an fp16 [rows][K] tensor folded into amax (fp32, K a multiple of 8).
+int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t st);
+
 int current_device();
 // Shared-memory opt-in of every kernel on the current device (call before any stream capture).
 int prepare_kernels();

@@ -91,6 +91,28 @@ __global__ void __launch_bounds__(LN_WARPS * 32, LN_BLOCKS_PER_SM)
     }
 }
 
+// Calibration: per-column max |x| over the rows of an fp16 [rows][K] tensor (K a multiple of 8), folded into amax
+// (fp32 bit patterns, which order like the non-negative values they hold) with atomicMax. One thread per 8 columns,
+// grid.y strides over the rows. The statistic of the reference's k_amax (kern_common.cuh:194-217).
+__global__ void __launch_bounds__(128) k_amax(const __half *__restrict__ x, int K, int rows, unsigned *__restrict__ amax)
+{
+    const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c8 * 8 >= K) return;
+    float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+        const uint4 v = __ldg((const uint4 *)(x + (size_t)r * K) + c8);
+        const __half2 *hv = (const __half2 *)&v;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 f = __half22float2(hv[j]);
+            m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
+            m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) atomicMax(amax + c8 * 8 + j, __float_as_uint(m[j]));
+}
+
 // Row statistics of the SwiGLU output for the folded MLP LayerNorm: the NSTAT partials (sum u, sum u^2) that fc1
 // wrote for a row are added in a fixed order (bit-identical run to run, as eva_kernels.cu:205-210) and turned into
 // (mean, rstd) over the 2730 units (eps 1e-6, k_fc2's formula, eva_kernels.cu:318-320), written in place into
