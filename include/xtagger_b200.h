@@ -198,9 +198,14 @@ int xtb_prep_ingest(uint8_t *rgba, int w, int h, int stride, int alpha, void *sc
 int xtb_prep_crop(const uint8_t *rgba, int w, int h, int stride, int x0, int y0, int cw, int ch, void *scratch,
                   uint16_t *out, void *stream);
 
-/* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). */
+/* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). The engine copies it
+ * back with every batch; eva_wait returns NULL (with an "eva:" line) for a batch after which it is set. */
 uint32_t xtb_error_word(int device);
 void xtb_error_clear(int device);
+/* Failure-path self-test on the current device: a kernel waits at most timeout_us (<= 10 s) on a barrier that is
+ * (arrive != 0) or is not arrived on; a wait that runs out sets bit 16 of the error word and the kernel returns
+ * normally. Nothing faults or hangs. */
+int xtb_selftest_wait(uint32_t timeout_us, int arrive, void *stream);
 
 #ifdef __cplusplus
 }

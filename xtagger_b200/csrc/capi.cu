@@ -203,6 +203,12 @@ int xtb_fc2_sp(const uint8_t *h8, int rows, const uint8_t *vals, const uint8_t *
     return launch_fc2_sp(A, W, ascale, rows, (__half *)x, (float2 *)stat, c, d, S(stream));
 }
 
+int xtb_selftest_wait(uint32_t timeout_us, int arrive, void *stream)
+{
+    if (timeout_us > 10000000u) return -1;  // at most 10 s
+    return launch_selftest_wait(timeout_us, arrive, S(stream));
+}
+
 uint32_t xtb_error_word(int device)
 {
     uint32_t *p = error_word(device), v = 0;

@@ -78,6 +78,7 @@ struct Replica {
     cudaStream_t cst = nullptr;
     cudaEvent_t in_ready[2] = {}, in_free[2] = {};
     int ib = 0;                         // input buffer of the next submit
+    uint32_t *errh = nullptr;           // pinned, per slot: the device error word after the slot's forward
 };
 
 struct Impl {
@@ -459,6 +460,8 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
         ECK(cudaEventCreateWithFlags(&r.in_ready[k], cudaEventDisableTiming));
         ECK(cudaEventCreateWithFlags(&r.in_free[k], cudaEventDisableTiming));
     }
+    ECK(cudaHostAlloc((void **)&r.errh, EVA_NBUF * sizeof(uint32_t), cudaHostAllocPortable));
+    memset(r.errh, 0, EVA_NBUF * sizeof(uint32_t));
     ECK(cudaStreamSynchronize(r.st));
     // capture the forward once per input buffer
     for (int k = 0; k < 2; k++) {
@@ -724,6 +727,8 @@ int eva_submit(eva *e, uint32_t buf, uint16_t *const *in, uint32_t n)
                 ECK(cudaMemcpyAsync(e->hpn[buf] + (size_t)off * D, r.pn, (size_t)cnt * D * 2, cudaMemcpyDeviceToHost,
                                     r.st));
         }
+        // the device error word after this forward (a bounded wait that ran out invalidates the batch)
+        ECK(cudaMemcpyAsync(r.errh + buf, error_word(r.dev), 4, cudaMemcpyDeviceToHost, r.st));
         ECK(cudaEventRecord(r.done[buf], r.st));
     }
     return 0;
@@ -747,6 +752,11 @@ const float *eva_wait(eva *e, uint32_t buf)
     for (Replica &r : im->reps) {
         cudaSetDevice(r.dev);
         if (cudaEventSynchronize(r.done[buf]) != cudaSuccess) return nullptr;
+        if (r.errh[buf]) {
+            fprintf(stderr, "eva: device %d: a kernel's bounded wait ran out (error bits 0x%x); slot %u is invalid "
+                            "(xtb_error_clear resets the device's error word)\n", r.dev, r.errh[buf], buf);
+            return nullptr;
+        }
     }
     return e->hout[buf];
 }
@@ -830,6 +840,7 @@ void eva_close(eva *e)
         void *bufs[] = {r.in, r.in_b, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp, r.spw};
         for (void *p : bufs)
             if (p) cudaFree(p);
+        if (r.errh) cudaFreeHost(r.errh);
         if (r.head_copy) {
             cudaFree(r.hw);
             cudaFree(r.hb);

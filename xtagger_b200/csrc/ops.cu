@@ -386,6 +386,13 @@ int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t 
     return 0;
 }
 
+int launch_selftest_wait(uint32_t timeout_us, int arrive, cudaStream_t st)
+{
+    k_selftest_wait<<<1, 32, 0, st>>>((uint64_t)timeout_us * 1000, arrive, error_word(current_device()));
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
                    float qs_head, cudaStream_t st)
 {

@@ -102,6 +102,9 @@ int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, _
 // Per-column max |x| of an fp16 [rows][K] tensor folded into amax (fp32, K a multiple of 8).
 int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t st);
 
+// Failure-path self-test: a wait of at most timeout_us on a barrier that is (arrive) or is not arrived on.
+int launch_selftest_wait(uint32_t timeout_us, int arrive, cudaStream_t st);
+
 int current_device();
 // Shared-memory opt-in of every kernel on the current device (call before any stream capture).
 int prepare_kernels();

@@ -18,6 +18,7 @@ enum : uint32_t {
     XTB_ERR_WAIT_TMEM = 2u,     // TMEM accumulator hand-off timed out
     XTB_ERR_WAIT_ATTN = 4u,     // attention pipeline timed out
     XTB_ERR_SHAPE = 8u,         // a launch was given a shape the kernel does not support
+    XTB_ERR_SELFTEST = 16u,     // the self-test's wait ran out (xtb_selftest_wait)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -76,6 +77,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 255u && globaltimer() - t0 > XTB_WAIT_NS) {
+            atomicOr(err, code);
+            return false;
+        }
+    }
+}
+
+// The same with the bound given in nanoseconds.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, uint32_t *err, uint32_t code, uint64_t ns)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && globaltimer() - t0 > ns) {
             atomicOr(err, code);
             return false;
         }

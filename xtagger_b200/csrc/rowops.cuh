@@ -113,6 +113,19 @@ __global__ void __launch_bounds__(128) k_amax(const __half *__restrict__ x, int 
     for (int j = 0; j < 8; j++) atomicMax(amax + c8 * 8 + j, __float_as_uint(m[j]));
 }
 
+// Self-test of the failure path: one thread waits on an mbarrier of count 1 with a bound of `ns`. With arrive set
+// it arrives first and the wait completes; without, nothing arrives, the wait runs out, XTB_ERR_SELFTEST is set in
+// the error word and the kernel returns normally (no trap, no fault: the context stays usable).
+__global__ void k_selftest_wait(uint64_t ns, int arrive, uint32_t *err)
+{
+    __shared__ uint64_t bar;
+    if (threadIdx.x) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (arrive) mbar_arrive(&bar);
+    mbar_wait_ns(&bar, 0, err, XTB_ERR_SELFTEST, ns);
+}
+
 // Row statistics of the SwiGLU output for the folded MLP LayerNorm: the NSTAT partials (sum u, sum u^2) that fc1
 // wrote for a row are added in a fixed order (bit-identical run to run, as eva_kernels.cu:205-210) and turned into
 // (mean, rstd) over the 2730 units (eps 1e-6, k_fc2's formula, eva_kernels.cu:318-320), written in place into

@@ -73,6 +73,7 @@ _SIGS = {
     "xtb_prep_crop": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P, _P]),
     "xtb_error_word": (C.c_uint32, [C.c_int]),
     "xtb_error_clear": (None, [C.c_int]),
+    "xtb_selftest_wait": (C.c_int, [C.c_uint32, C.c_int, _P]),
 }
 
 
