@@ -36,11 +36,14 @@ def models(tmp_path_factory):
         # 2:4-pruned projections (config 5): the engine runs them on the sparse tensor-core kernels
         "v4_l2_p": M.write_synthetic(os.path.join(d, "e.bin"), seed=8, nl=2, ln_noise=1.0, head_fp8=True, prune24=True),
         "v4_l24_p": M.write_synthetic(os.path.join(d, "f.bin"), seed=9, nl=24, head_fp8=True, prune24=True),
+        # the reference's format pruned as prune24.py does: the sparse kernels without block-scale promotion
+        "v3_l24_p": M.write_synthetic(os.path.join(d, "g.bin"), seed=10, nl=24, version=3, head_fp8=False,
+                                      prune24=True),
     }
 
 
 @pytest.mark.parametrize("name,nimg", [("v4_l2_h8", 3), ("v4_l2_h16", 2), ("v4_l24_h8", 1), ("v3_l24", 1),
-                                       ("v4_l2_p", 3), ("v4_l24_p", 1)])
+                                       ("v4_l2_p", 3), ("v4_l24_p", 1), ("v3_l24_p", 1)])
 def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     from oracle import oracle as O
     from xtagger_b200 import model as M

@@ -388,6 +388,7 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
                     sparse24_bytes(L.w[g].n, L.w[g].k, &moff);
                     const uint8_t *v = r.spw + im->sp_off[(size_t)i * NG + g];
                     RCK(make_sparse_weight(&L.sw[g], v, v + moff, L.w[g].n, L.w[g].k, L.w[g].ws));
+                    L.sw[g].uniform = L.w[g].uniform;  // v3: one scale per tensor
                 }
         ECK(cudaStreamSynchronize(r.st));  // the host buffer is pageable
     }

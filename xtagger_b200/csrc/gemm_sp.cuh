@@ -22,6 +22,9 @@
 // loop instead of stalling it. Block scales are promoted per K block as gemm.cuh does.
 // TMEM: four accumulators of 112 columns (group g: 2g and 2g + 1, ping-pong per K block) at [0, 448), metadata at
 // 448 and 452 (ping-pong per K block; a metadata column must be even).
+// Without PROMOTE (a weight with one scale for the whole tensor, as prune24.py writes the reference's v3 files) a
+// tile accumulates its whole K range in one of its group's two buffers, which then ping-pong per tile: the group
+// drains and scales the tile once, and its apply overlaps both the other group's tile and its own next tile.
 #pragma once
 #include "gemm.cuh"
 #include "ops.h"
@@ -56,6 +59,7 @@ struct SpArgs {
     const float *ws;  // block scales [ws_rows][ws_ld] (row = 128-row weight block)
     int ws_ld, ws_rows;
     float ascale;     // activation dequant scale
+    float wsu;        // without PROMOTE: the weight's one scale
     uint32_t *err;
 };
 
@@ -76,7 +80,7 @@ struct SpNoBars {
     __device__ __forceinline__ static void init_bars(uint64_t *) {}
 };
 
-template <class Epi>
+template <class Epi, bool PROMOTE = true>
 __global__ void __launch_bounds__(SpCfg::THREADS, 1)
     k_gemm_sp(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmE,
               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC, const SpArgs g,
@@ -159,8 +163,10 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
                 for (int k = 0; k < KI; k++) {
                     const uint32_t c = cnt[grp];
                     const int buf = 2 * grp + (int)(c & 1);
-                    if (!(ok = mbar_wait(&tempty[buf], ((c >> 1) & 1) ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
-                    tc_fence_after();
+                    if (PROMOTE || k == 0) {
+                        if (!(ok = mbar_wait(&tempty[buf], ((c >> 1) & 1) ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
+                        tc_fence_after();
+                    }
                     if (!(ok = mbar_wait(&full[stage], ph, g.err, XTB_ERR_WAIT_TMA))) break;
                     tc_fence_after();
                     const uint32_t ecol = tbase + C::E_COL + 4 * eb;
@@ -171,11 +177,13 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 2; kk++)
                         umma_sp(d, sdesc(a0 + kk * 32, 512, SWZ_64B), sdesc(b0 + kk * 64, 1024, SWZ_128B), ecol + 2 * kk,
-                                IDESC, kk > 0);
+                                IDESC, PROMOTE ? (kk > 0) : (k > 0 || kk > 0));
                     umma_commit(&empty[stage]);
-                    umma_commit(&tfull[buf]);
                     eb ^= 1;
-                    cnt[grp] = c + 1;
+                    if (PROMOTE || k == KI - 1) {
+                        umma_commit(&tfull[buf]);
+                        cnt[grp] = c + 1;
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1;
@@ -208,12 +216,13 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
             float2 acc[SP_COLS / 2];
 #pragma unroll
             for (int j = 0; j < SP_COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);
-            const float *wsr = g.ws + (size_t)min(nb, g.ws_rows - 1) * g.ws_ld;
-            float snext = __ldg(wsr);
+            const float *wsr = PROMOTE ? g.ws + (size_t)min(nb, g.ws_rows - 1) * g.ws_ld : nullptr;
+            float snext = PROMOTE ? __ldg(wsr) : g.wsu;
             const float amul = g.ascale * Epi::row_scale(ep, cx.f0);
-            for (int u = 0; u < KI; u++, c++) {
+            const int units = PROMOTE ? KI : 1;
+            for (int u = 0; u < units; u++, c++) {
                 const float s = amul * snext;
-                if (u + 1 < KI) snext = __ldg(wsr + u + 1);
+                if (PROMOTE && u + 1 < units) snext = __ldg(wsr + u + 1);
                 const int buf = 2 * grp + (int)(c & 1);
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[buf], (c >> 1) & 1, g.err, XTB_ERR_WAIT_TMEM)))) break;
                 tc_fence_after();
@@ -225,7 +234,9 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
                     tmem_ld16(taddr + cc * 16, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 8; j++) acc[cc * 8 + j] = ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[cc * 8 + j]);
+                    for (int j = 0; j < 8; j++)
+                        acc[cc * 8 + j] = PROMOTE ? ffma2(s2, make_float2(v[2 * j], v[2 * j + 1]), acc[cc * 8 + j])
+                                                  : mul2(s2, make_float2(v[2 * j], v[2 * j + 1]));
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -329,23 +340,39 @@ struct SpQKV {
         const uint8_t *ang = angles(cx) + (cx.lane >> 1) * 8;
         if (which < 2 && !__all_sync(0xffffffffu, mbar_wait(&cx.ebar[h], cx.use & 1, cx.err, XTB_ERR_WAIT_TMEM)))
             return false;
-        uint8_t *dst = (which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8) + dbase + cx.lane;
-        int b = cx.t0 / T, tt = cx.t0 - b * T;
+        uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
+        // E4M3 bytes of 56 tokens x 32 dims are staged per warp in its slice of the (otherwise unused) exchange area,
+        // then leave as 16-byte pieces
+        uint8_t *ob = (uint8_t *)cx.xred + (cx.quad & 3) * (SP_COLS / 2) * 32;
+        int tt = cx.t0 % T;
 #pragma unroll
-        for (int j = 0; j < SP_COLS; j++) {
-            float v = acc[j];
-            const bool live = cx.t0 + j < p.M;
-            if (which < 2) {
-                // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin); cls rows and rows past M: cos 1, sin 0
-                const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
-                float2 c = make_float2(1.f, 0.f);
-                if (tt > 0 && live) c = *(const float2 *)(ang + j * 128);
-                v = fmaf(pv, odd ? c.y : -c.y, v * c.x);
+        for (int hf = 0; hf < 2; hf++) {
+            __syncwarp();
+#pragma unroll
+            for (int jj = 0; jj < SP_COLS / 2; jj++) {
+                const int j = hf * (SP_COLS / 2) + jj;
+                float v = acc[j];
+                if (which < 2) {
+                    // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin); cls rows and rows past M: cos 1, sin 0
+                    const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
+                    float2 c = make_float2(1.f, 0.f);
+                    if (tt > 0 && cx.t0 + j < p.M) c = *(const float2 *)(ang + j * 128);
+                    v = fmaf(pv, odd ? c.y : -c.y, v * c.x);
+                }
+                ob[jj * 32 + cx.lane] = (uint8_t)e4m3x2(v, 0.f);
+                if (++tt == T) tt = 0;
             }
-            if (live) dst[((size_t)(b * NH + head) * TP + tt) << 6] = (uint8_t)e4m3x2(v, 0.f);
-            if (++tt == T) {
-                tt = 0;
-                ++b;
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < (SP_COLS + 31) / 32; i++) {  // 56 tokens x 2 pieces of 16 bytes: 112 of 128 lanes
+                const int pc = i * 32 + cx.lane;
+                const int r = pc >> 1, ch = pc & 1;
+                const int t = cx.t0 + hf * (SP_COLS / 2) + r;
+                if (r < SP_COLS / 2 && t < p.M) {
+                    const int b = t / T, tq = t - b * T;
+                    *(uint4 *)(dst + (((size_t)(b * NH + head) * TP + tq) << 6) + dbase + 16 * ch) =
+                        *(const uint4 *)(ob + r * 32 + 16 * ch);
+                }
             }
         }
         if (which < 2) {

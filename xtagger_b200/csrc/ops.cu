@@ -297,11 +297,11 @@ int make_sparse_weight(SparseW *w, const uint8_t *vals, const uint8_t *meta, int
 }
 
 // One launch of the sparse GEMM: persistent grid of one CTA per SM over (weight tile, token tile) pairs.
-template <class Epi>
-static int run_gemm_sp(const SparseW &w, const Operand &x, int M, float ascale, const typename Epi::Params &ep,
-                       cudaStream_t st, const CUtensorMap *tmc = nullptr)
+template <class Epi, bool PROMOTE>
+static int run_gemm_sp_k(const SparseW &w, const Operand &x, int M, float ascale, const typename Epi::Params &ep,
+                         cudaStream_t st, const CUtensorMap *tmc)
 {
-    auto kern = k_gemm_sp<Epi>;
+    auto kern = k_gemm_sp<Epi, PROMOTE>;
     if (set_smem((const void *)kern, SpCfg::SMEM)) return -1;
     if (x.row_bytes != w.k || x.box_rows != SP_BOX_ROWS || M <= 0 || M > x.rows) {
         fprintf(stderr, "eva: sparse gemm operands (K bytes %d vs %d, box %d rows, M %d of %d)\n", x.row_bytes, w.k,
@@ -318,6 +318,7 @@ static int run_gemm_sp(const SparseW &w, const Operand &x, int M, float ascale, 
     g.ws_ld = kb(w.k);
     g.ws_rows = kb(w.n);
     g.ascale = ascale;
+    g.wsu = w.uniform;
     g.err = error_word(dev);
     const int total = g.n_tiles * g.t_tiles;
     int grid = num_sms(dev);
@@ -325,6 +326,14 @@ static int run_gemm_sp(const SparseW &w, const Operand &x, int M, float ascale, 
     kern<<<grid, SpCfg::THREADS, SpCfg::SMEM, st>>>(w.va, w.me, x.map, tmc ? *tmc : x.map, g, ep);
     XTB_CK(cudaGetLastError());
     return 0;
+}
+
+template <class Epi>
+static int run_gemm_sp(const SparseW &w, const Operand &x, int M, float ascale, const typename Epi::Params &ep,
+                       cudaStream_t st, const CUtensorMap *tmc = nullptr)
+{
+    if (w.uniform > 0.0f) return run_gemm_sp_k<Epi, false>(w, x, M, ascale, ep, st, tmc);
+    return run_gemm_sp_k<Epi, true>(w, x, M, ascale, ep, st, tmc);
 }
 
 int launch_gemm_sp_f32(const Operand &x, const SparseW &w, float ascale, float *out, int ldo, cudaStream_t st)
@@ -435,9 +444,11 @@ int prepare_kernels()
                          (const void *)k_gemm<EpiHead<32>, 64, false, true, true>};
     for (const void *k : g64)
         if (set_smem(k, GemmCfg<64>::SMEM)) return -1;
-    const void *sp[] = {(const void *)k_gemm_sp<SpF32>, (const void *)k_gemm_sp<SpQKV>,
-                        (const void *)k_gemm_sp<SpResid<false>>, (const void *)k_gemm_sp<SpResid<true>>,
-                        (const void *)k_gemm_sp<SpFC1>};
+    const void *sp[] = {(const void *)k_gemm_sp<SpF32, true>,          (const void *)k_gemm_sp<SpQKV, true>,
+                        (const void *)k_gemm_sp<SpResid<false>, true>, (const void *)k_gemm_sp<SpResid<true>, true>,
+                        (const void *)k_gemm_sp<SpFC1, true>,          (const void *)k_gemm_sp<SpF32, false>,
+                        (const void *)k_gemm_sp<SpQKV, false>,         (const void *)k_gemm_sp<SpResid<false>, false>,
+                        (const void *)k_gemm_sp<SpResid<true>, false>, (const void *)k_gemm_sp<SpFC1, false>};
     for (const void *k : sp)
         if (set_smem(k, SpCfg::SMEM)) return -1;
     if (set_smem((const void *)k_ln_e4m3, LN_SMEM)) return -1;

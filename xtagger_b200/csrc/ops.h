@@ -80,6 +80,7 @@ struct SparseW {
     CUtensorMap va, me;
     const float *ws;
     int n, k, np, kp;
+    float uniform = 0.0f;  // > 0: every block scale equals it (no per-K-block promotion, see Weight8)
 };
 // Box height of the activation operand of the sparse kernels (tokens per tile).
 constexpr int SP_BOX_ROWS = 112;
