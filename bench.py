@@ -9,6 +9,10 @@ head): the GEMMs then accumulate the whole K range in TMEM and scale once, as th
 the format oracle/ref_time.py times the reference's kernels on.
 --sparse is config 5: the four projections of every layer 2:4-pruned by magnitude (prune24.py's rule), which the
 engine runs on the sparse tensor cores (tcgen05.mma.sp); global batch 128 unless --batch is given.
+--nt 13461 --batch 32 is config 4 (implies --mix): the inputs are views of seeded 896^2 sources (per source the
+whole image and its four quadrants, 6 x 5 + 2 whole images), made by the GPU preprocessing, and the line gains
+e2e_decoded: images/s from decoded RGBX sources in pinned host memory through H2D, the preprocessing kernels, the
+forward and the scores' D2H, all on the engine's stream.
 
 Prints one JSON line (rank 0):
   value       whole-job images/s with inputs resident on the devices (CUDA events around K graph launches on the
@@ -23,6 +27,7 @@ Prints one JSON line (rank 0):
 own and its host engine is Windows-only) on the same config and prints the same line with "impl": "reference".
 """
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -153,6 +158,7 @@ def run_ours(args, rank, world, local):
     import torch
     from xtagger_b200 import model as M
     from xtagger_b200.engine import Engine
+    from xtagger_b200.lib import EVA_IN
 
     torch.cuda.set_device(local)
     pg = None
@@ -170,8 +176,26 @@ def run_ours(args, rank, world, local):
     model = model_path(rank, world, barrier)
     lo, hi = shard_bounds(args.batch, world, rank)
     nb = hi - lo
-    allx = M.synthetic_inputs(args.batch, seed=1)
-    pool = np.ascontiguousarray(allx[lo:hi])
+    dev = torch.device("cuda", local)
+    if args.mix:
+        # config 4: the whole images and quadrant crops of 896^2 sources, resampled on the device by the GPU
+        # preprocessing (the same kernels the decoded-image e2e below times)
+        from xtagger_b200 import views as V
+        views_all = V.mix_views(args.batch)
+        views = views_all[lo:hi]
+        nsrc = V.num_sources(views_all)
+        used = sorted({v[0] for v in views})
+        src_host = torch.from_numpy(V.mix_sources(nsrc, seed=1)).pin_memory()
+        src_dev = src_host.to(dev)
+        src_ptrs = [src_dev[i].data_ptr() for i in range(nsrc)]
+        prep = V.DevicePrep(V.SIDE, V.SIDE, nsrc, device=dev)
+        ops = torch.empty((max(nb, 1), EVA_IN), dtype=torch.int16, device=dev)
+        prep.run(src_ptrs, views, ops.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+        torch.cuda.synchronize()
+        pool = np.ascontiguousarray(ops[:nb].cpu().numpy().view(np.uint16).reshape(nb, 1024, 592))
+    else:
+        allx = M.synthetic_inputs(args.batch, seed=1)
+        pool = np.ascontiguousarray(allx[lo:hi])
     eng = Engine(model, devices=(local,), nb=nb, pool=pool)
     eng.ready()
     st = torch.cuda.ExternalStream(eng.stream(0), device=torch.device("cuda", local))
@@ -218,6 +242,48 @@ def run_ours(args, rank, world, local):
     barrier()
     e2e = args.batch * args.steps / te
 
+    # ---- config 4, end to end from decoded images: every step copies the 896^2 RGBX sources from pinned host memory,
+    # preprocesses them on the device into the engine's resident inputs (xtb_prep_ingest / xtb_prep_crop), runs the
+    # forward and copies the scores back to pinned host memory; all on the engine's stream, timed by CUDA events ----
+    decoded = None
+    if args.mix:
+        from xtagger_b200 import lib as XL
+        xl = XL.lib()
+        din, dout, est = eng.device_input(0), eng.device_output(0), eng.stream(0)
+        scores = torch.empty((max(nb, 1), eng.nt), dtype=torch.float32).pin_memory()
+        nk = [0]
+
+        def dstep():
+            for i in used:
+                XL.check(xl.xtb_copy_async(ctypes.c_void_p(src_ptrs[i]), ctypes.c_void_p(src_host[i].data_ptr()),
+                                           src_host[i].numel(), ctypes.c_void_p(est)), "xtb_copy_async")
+            nk[0] = prep.run(src_ptrs, views, din, est)
+            eng.forward_resident()
+            XL.check(xl.xtb_copy_async(ctypes.c_void_p(scores.data_ptr()), ctypes.c_void_p(dout), nb * eng.nt * 4,
+                                       ctypes.c_void_p(est)), "xtb_copy_async")
+
+        for _ in range(args.warmup):
+            dstep()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(args.steps):
+            dstep()
+        e1.record(st)
+        torch.cuda.synchronize()
+        td = allmax(e0.elapsed_time(e1) / 1e3)
+        barrier()
+        # the scores of the last step equal the resident forward's on the same inputs (prep is deterministic)
+        assert np.isfinite(scores[:nb].numpy()).all()
+        decoded = {"value": args.batch * args.steps / td, "unit": "images/s",
+                   "h2d_bytes_per_step": sum(src_host[i].numel() for i in used) * world,
+                   "d2h_bytes_per_step": args.batch * eng.nt * 4,
+                   "prep_kernels_per_step": nk[0] * world,
+                   "what": "decoded 896^2 RGBX sources (pinned host) -> H2D -> GPU preprocessing (whole image: "
+                           "antialiased bicubic 896 -> 448; quadrants: normalise) -> forward -> scores D2H, CUDA "
+                           "events on the engine stream, max over ranks"}
+
     # ---- roofline of the dominant kernel (fc1) from one direct forward with per-kernel events ----
     prof = eng.profile()
     sparse_kinds = eng.sparse_kinds()
@@ -240,7 +306,10 @@ def run_ours(args, rank, world, local):
                 "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
                 "config": {"workload": f"{config_name(args)}: EVA02-L 448^2 forward (24 layers, d 1024, 1025 tokens, {args.nt}-tag "
-                                       f"{'fp16' if args.v3 else 'FP8'} head), global batch split across the GPUs",
+                                       f"{'fp16' if args.v3 else 'FP8'} head), global batch split across the GPUs" +
+                                       (f"; inputs: {len(views_all)} views of {nsrc} seeded 896^2 sources (whole "
+                                        "image + 4 quadrant crops per source, the rest whole images), "
+                                        "preprocessed on the device" if args.mix else ""),
                            "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
                            "weights": ("random-init, E4M3 with one fp32 scale per tensor (eva02.bin v3), fp16 head"
                                        if args.v3 else "random-init, E4M3 with fp32 scales per 128x128 block") +
@@ -258,6 +327,7 @@ def run_ours(args, rank, world, local):
                              "traffic": None if fc1_sparse else FC1_TRAFFIC_PER_ROW * rows,
                              "traffic_unit": "bytes per launch (ncu DRAM read + write at batch 32, scaled by rows)"},
                 "forward_tflops": FLOP_PER_IMAGE * value / 1e12,
+                "e2e_decoded": decoded,
                 "profile_ms": prof,
                 "clocks": clocks,
                 "gpu_launches": launches * args.steps * world}
@@ -295,11 +365,15 @@ def main():
     ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
     ap.add_argument("--sparse", action="store_true", help="config 5: 2:4-pruned projections on the sparse kernels")
     ap.add_argument("--v3", action="store_true", help="weights in the reference's v3 format (per-tensor scales)")
+    ap.add_argument("--mix", action="store_true",
+                    help="inputs: whole images + quadrant crops of 896^2 sources, preprocessed on the device (the "
+                         "default for config 4: --nt 13461 --batch 32)")
     args = ap.parse_args()
     rank, world, local = dist_env()
     MODEL_KW["nt"] = args.nt
     if args.batch is None:
         args.batch = 128 if args.sparse else 64
+    args.mix = args.mix or (args.nt == 13461 and args.batch == 32)
     if args.v3:
         MODEL_KW.update(version=3, head_fp8=False)
     if args.sparse:

@@ -92,6 +92,11 @@ int eva_upload(eva *e, uint16_t *const *in, uint32_t n);
 int eva_download(eva *e, float *out, uint32_t n);
 /* The CUDA stream (cudaStream_t) the engine uses on its i-th device; NULL if out of range. */
 void *eva_stream(eva *e, int i);
+/* Device addresses of the i-th device's resident batch: the inputs [nb_i][EVA_IN] halves that eva_forward_resident
+ * reads (a producer on that device, such as xtb_prep_crop ordered on eva_stream(e, i), may write them in place of
+ * eva_upload) and the scores [nb_i][nt] floats it writes. nb_i is that device's share of nb. NULL if out of range. */
+void *eva_input(eva *e, int i);
+void *eva_output(eva *e, int i);
 /* Number of kernel launches in one forward on one device. */
 int eva_launches_per_forward(eva *e);
 /* Projection kinds running on the 2:4-sparse tensor-core kernels (bit 0 QKV, 1 O, 2 W12, 3 W2): with XTB_SPARSE=1 in
@@ -197,6 +202,13 @@ size_t xtb_prep_scratch_bytes(int w, int h);
 int xtb_prep_ingest(uint8_t *rgba, int w, int h, int stride, int alpha, void *scratch, void *stream);
 int xtb_prep_crop(const uint8_t *rgba, int w, int h, int stride, int x0, int y0, int cw, int ch, void *scratch,
                   uint16_t *out, void *stream);
+/* Kernels one call launches: xtb_prep_crop of that rect, or xtb_prep_ingest of a w x h image when cw <= 0; -1 on a
+ * bad rect. */
+int xtb_prep_kernels(int w, int h, int x0, int y0, int cw, int ch);
+
+/* One stream-ordered copy of `bytes` between any two of host (pinned for asynchrony) and device memory, for hosts
+ * with no CUDA binding of their own (e.g. scores of eva_output back to the host after a device-side batch). */
+int xtb_copy_async(void *dst, const void *src, size_t bytes, void *stream);
 
 /* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). The engine copies it
  * back with every batch; eva_wait returns NULL (with an "eva:" line) for a batch after which it is set. */

@@ -121,3 +121,27 @@ def test_resample_matches_float64_filter(O, w, h):
         plane = o[:, :, q * 196:(q + 1) * 196].reshape(32, 32, 14, 14).transpose(0, 2, 1, 3).reshape(448, 448)
         got = plane.view(np.float16).astype(np.float64)
         assert np.abs(got - want[..., c]).max() <= 2.5e-3  # fp16 steps of 2^-11 near 1 plus fp32 sums
+
+
+def test_mix_views_layout():
+    """32 inputs = 6 sources x (whole image + 4 quadrants) + 2 whole images, every rect inside its 896^2 source."""
+    from xtagger_b200 import views as V
+    v = V.mix_views(32)
+    assert len(v) == 32 and V.num_sources(v) == 8
+    assert sum(1 for x in v if x[3] == V.SIDE) == 8
+    for s in range(6):
+        quads = sorted((x0, y0) for (t, x0, y0, cw, ch) in v if t == s and cw == V.SIDE // 2)
+        assert quads == [(0, 0), (0, 448), (448, 0), (448, 448)]
+    assert all(0 <= x0 and 0 <= y0 and x0 + cw <= V.SIDE and y0 + ch <= V.SIDE for _, x0, y0, cw, ch in v)
+    src = V.mix_sources(2, seed=3)
+    assert src.shape == (2, 896, 896 * 4) and (src.reshape(2, 896, 896, 4)[..., 3] == 255).all()
+
+
+@pytest.mark.parametrize("args,n", [((896, 896, 0, 0, 0, 0), 1), ((4000, 3000, 0, 0, 0, 0), 3),
+                                    ((896, 896, 0, 0, 896, 896), 3), ((896, 896, 448, 448, 448, 448), 1),
+                                    ((897, 897, 100, 200, 448, 448), 1), ((896, 896, 500, 0, 448, 10), -1),
+                                    ((0, 896, 0, 0, 0, 0), -1)])
+def test_prep_kernel_counts(xlib, args, n):
+    """Kernels per call: ingest = alpha pass + one per pyramid level above 0; crop = 1 on the normalise-only path,
+    3 (tables, vertical, horizontal) when resampling; bad rects -1. Host arithmetic only, no device."""
+    assert xlib.xtb_prep_kernels(*args) == n

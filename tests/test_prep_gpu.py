@@ -63,3 +63,61 @@ def test_prep_rejects_bad_arguments(xlib, cuda):
     assert xlib.xtb_prep_ingest(G.P(img), 10, 10, 38, 0, G.P(scratch), None) == -1      # stride < 4 w
     assert xlib.xtb_prep_crop(G.P(img), 10, 10, 40, 5, 0, 6, 10, G.P(scratch), G.P(out), None) == -1  # rect
     assert xlib.xtb_prep_crop(G.P(img), 10, 10, 40, 0, 0, 10, 10, None, G.P(out), None) == -1
+
+
+def test_mixed_views_match_oracle(xlib, cuda):
+    """The PixAI-style batch (whole images and quadrant crops of 896^2 sources, xtagger_b200.views) made on the
+    device equals the oracle's preprocessing of every view."""
+    from oracle import oracle as O
+    from xtagger_b200 import views as V
+    views = V.mix_views(7)  # one source x (whole + 4 quadrants), then two whole images
+    nsrc = V.num_sources(views)
+    src = V.mix_sources(nsrc, seed=9)
+    dsrc = G.dev(src)
+    prep = V.DevicePrep(V.SIDE, V.SIDE, nsrc)
+    out = G.zeros((len(views), 1024 * 592), __import__("torch").int16)
+    nk = prep.run([dsrc[i].data_ptr() for i in range(nsrc)], views, out.data_ptr(), 0)
+    assert nk == nsrc * 1 + 3 * 3 + 4 * 1  # ingest 1 each; whole images 3 kernels; quadrants 1
+    got = G.host(out).view(np.uint16)
+    for i, (s, x0, y0, cw, ch) in enumerate(views):
+        want = np.zeros(1024 * 592, np.uint16)
+        O.lib().or_prep(src[s].copy(), V.SIDE, V.SIDE, 4 * V.SIDE, 0, x0, y0, cw, ch, want)
+        assert np.array_equal(got[i], want), f"view {i} {views[i]} differs"
+
+
+def test_prep_feeds_engine_in_place(xlib, cuda, tmp_path):
+    """Preprocessing written straight into the engine's resident inputs (eva_input) and the scores read back from
+    eva_output (xtb_copy_async) give the same scores as eva_submit of the same inputs from the host."""
+    import torch
+    from xtagger_b200 import lib as L
+    from xtagger_b200 import model as M
+    from xtagger_b200 import views as V
+    from xtagger_b200.engine import Engine
+    path = M.write_synthetic(str(tmp_path / "m.bin"), seed=7, nl=2, nt=300, ln_noise=1.0)
+    views = V.mix_views(5)
+    src = V.mix_sources(1, seed=10)
+    dsrc = G.dev(src)
+    prep = V.DevicePrep(V.SIDE, V.SIDE, 1)
+    eng = Engine(path, nb=len(views))
+    try:
+        eng.ready()
+        st = eng.stream(0)
+        prep.run([dsrc[0].data_ptr()], views, eng.device_input(0), st)
+        eng.forward_resident()
+        scores = torch.empty((len(views), eng.nt), dtype=torch.float32).pin_memory()
+        assert xlib.xtb_copy_async(C.c_void_p(scores.data_ptr()), C.c_void_p(eng.device_output(0)),
+                                   scores.numel() * 4, C.c_void_p(st)) == 0
+        torch.cuda.synchronize()
+        got = scores.numpy().copy()
+        ops = np.zeros((len(views), 1024, 592), np.uint16)
+        torch.cuda.synchronize()
+        assert xlib.xtb_copy_async(C.c_void_p(ops.ctypes.data), C.c_void_p(eng.device_input(0)),
+                                   ops.nbytes, C.c_void_p(st)) == 0
+        torch.cuda.synchronize()
+        want = eng.run(ops)
+        assert eng.device_input(1) is None and eng.device_output(-1) is None
+    finally:
+        eng.close()
+    assert np.isfinite(got).all()
+    assert np.array_equal(got, want)
+    assert L.EVA_IN == 1024 * 592

@@ -209,6 +209,12 @@ int xtb_selftest_wait(uint32_t timeout_us, int arrive, void *stream)
     return launch_selftest_wait(timeout_us, arrive, S(stream));
 }
 
+int xtb_copy_async(void *dst, const void *src, size_t bytes, void *stream)
+{
+    if (!dst || !src) return -1;
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, S(stream)) == cudaSuccess ? 0 : -1;
+}
+
 uint32_t xtb_error_word(int device)
 {
     uint32_t *p = error_word(device), v = 0;

@@ -913,6 +913,20 @@ void *eva_stream(eva *e, int i)
     return (void *)im->reps[i].st;
 }
 
+void *eva_input(eva *e, int i)
+{
+    Impl *im = I(e);
+    if (!im || eva_ready(e) || i < 0 || (size_t)i >= im->reps.size()) return nullptr;
+    return (void *)im->reps[i].in;
+}
+
+void *eva_output(eva *e, int i)
+{
+    Impl *im = I(e);
+    if (!im || eva_ready(e) || i < 0 || (size_t)i >= im->reps.size()) return nullptr;
+    return (void *)im->reps[i].out;
+}
+
 int eva_sparse_kinds(eva *e)
 {
     if (eva_ready(e)) return -1;

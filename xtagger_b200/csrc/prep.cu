@@ -259,19 +259,25 @@ int prep_ingest(uint8_t *img, int w, int h, int stride, int alpha, uint8_t *scra
     return 0;
 }
 
-int prep_crop(const uint8_t *img, int w, int h, int stride, int x0, int y0, int cw, int ch, uint8_t *scratch,
-              uint16_t *out, cudaStream_t st)
+// The pyramid level a crop reads and the rect on it (clipped, at least one pixel); returns the level.
+static int crop_level(const Pyr &p, int &x0, int &y0, int &cw, int &ch)
 {
-    const Pyr p = pyr_dims(w, h);
     const int side0 = std::max(cw, ch);
     int L = 0;
     while (L + 1 < p.n && (side0 >> (L + 1)) >= 2 * PREP_S) L++;
-    // the rect on level L (clipped, at least one pixel)
     int x1 = std::min((x0 + cw) >> L, p.lw[L]), y1 = std::min((y0 + ch) >> L, p.lh[L]);
     x0 = std::min(x0 >> L, p.lw[L] - 1);
     y0 = std::min(y0 >> L, p.lh[L] - 1);
     cw = x1 > x0 ? x1 - x0 : 1;
     ch = y1 > y0 ? y1 - y0 : 1;
+    return L;
+}
+
+int prep_crop(const uint8_t *img, int w, int h, int stride, int x0, int y0, int cw, int ch, uint8_t *scratch,
+              uint16_t *out, cudaStream_t st)
+{
+    const Pyr p = pyr_dims(w, h);
+    const int L = crop_level(p, x0, y0, cw, ch);
     const int ls = L == 0 ? stride : p.lw[L] * 4;
     const uint8_t *src = (L == 0 ? img : scratch + p.off[L]) + (size_t)y0 * ls + (size_t)x0 * 4;
     const int side = std::max(cw, ch);
@@ -337,6 +343,16 @@ int xtb_prep_crop(const uint8_t *rgba, int w, int h, int stride, int x0, int y0,
         return -1;
     }
     return prep_crop(rgba, w, h, stride, x0, y0, cw, ch, (uint8_t *)scratch, out, (cudaStream_t)stream);
+}
+
+int xtb_prep_kernels(int w, int h, int x0, int y0, int cw, int ch)
+{
+    if (w <= 0 || h <= 0) return -1;
+    const Pyr p = pyr_dims(w, h);
+    if (cw <= 0) return p.n;  // xtb_prep_ingest: alpha over white, then one box-halving kernel per level
+    if (x0 < 0 || y0 < 0 || ch <= 0 || x0 + cw > w || y0 + ch > h) return -1;
+    crop_level(p, x0, y0, cw, ch);
+    return std::max(cw, ch) == PREP_S ? 1 : 3;  // normalise only, or weight tables + vertical + horizontal pass
 }
 
 }  // extern "C"

@@ -98,6 +98,14 @@ class Engine:
     def stream(self, i=0):
         return self.lib.eva_stream(C.byref(self.e), i)
 
+    def device_input(self, i=0):
+        """Device address of the i-th device's resident inputs (what forward_resident reads)."""
+        return self.lib.eva_input(C.byref(self.e), i)
+
+    def device_output(self, i=0):
+        """Device address of the i-th device's resident scores (what forward_resident writes)."""
+        return self.lib.eva_output(C.byref(self.e), i)
+
     def launches_per_forward(self):
         return self.lib.eva_launches_per_forward(C.byref(self.e))
 

@@ -44,6 +44,8 @@ _SIGS = {
     "eva_upload": (C.c_int, [C.POINTER(Eva), C.POINTER(_P), C.c_uint32]),
     "eva_download": (C.c_int, [C.POINTER(Eva), _P, C.c_uint32]),
     "eva_stream": (_P, [C.POINTER(Eva), C.c_int]),
+    "eva_input": (_P, [C.POINTER(Eva), C.c_int]),
+    "eva_output": (_P, [C.POINTER(Eva), C.c_int]),
     "eva_launches_per_forward": (C.c_int, [C.POINTER(Eva)]),
     "eva_sparse_kinds": (C.c_int, [C.POINTER(Eva)]),
     "eva_profile": (C.c_int, [C.POINTER(Eva), _P, C.c_int]),
@@ -71,6 +73,8 @@ _SIGS = {
     "xtb_prep_scratch_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "xtb_prep_ingest": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P]),
     "xtb_prep_crop": (C.c_int, [_P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _P, _P, _P]),
+    "xtb_prep_kernels": (C.c_int, [C.c_int] * 6),
+    "xtb_copy_async": (C.c_int, [_P, _P, C.c_size_t, _P]),
     "xtb_error_word": (C.c_uint32, [C.c_int]),
     "xtb_error_clear": (None, [C.c_int]),
     "xtb_selftest_wait": (C.c_int, [C.c_uint32, C.c_int, _P]),
