@@ -219,6 +219,55 @@ void xtb_error_clear(int device);
  * normally. Nothing faults or hangs. */
 int xtb_selftest_wait(uint32_t timeout_us, int arrive, void *stream);
 
+/* ---- PixAI engine (px_*): a drop-in for src/engine/px.h (ViTDet-L tagger at 1008^2, 30877 tags) ----
+ * Input per model input (px.h:9-10): fp16 [5184 window-major patches][592], RGB c * 196 + ky * 14 + kx, [-1, 1],
+ * columns 588..591 zero. Weights: pixai.bin v3 (export_pixai.py with a calibration file: E4M3 with one scale per
+ * tensor); header words 4 / 5 (zero in the reference's files) may give the number of blocks and the mask of global
+ * blocks. Errors: 0 / -1 / NULL with a "px: ..." line on stderr, as the reference. */
+#ifndef PX_NB
+#define PX_NB 4                               /* model inputs per submit (px.h:19-21) */
+#endif
+#define PX_NBUF 4                             /* host output slots (px.h:27) */
+#define PX_NL 32
+#define PX_IN ((size_t)5184 * EVA_K0P)        /* halves per model input (px.h:33) */
+
+/* Engine handle, caller-allocated like the reference's `px` (px.h:59-89); impl holds the rest. */
+typedef struct px {
+    uint32_t nt, ntp;                         /* tags (and rounded up to 8) */
+    uint32_t nb;                              /* model inputs per submit */
+    float *hout[PX_NBUF];                     /* per slot: scores [nb][nt] fp32, engine-owned */
+    void *impl;
+} px;
+
+/* Replaces px_open (px.h:355-384): validate the header, start the bring-up on its own thread, return at once.
+ * `pool` (poolb bytes): the caller's input pool, page-locked in place by the bring-up. */
+int px_open(px *p, const char *weights, int device, void *pool, size_t poolb);
+/* Same with nb inputs per submit (no counterpart in the reference, which fixes PX_NB). */
+int px_open_ex(px *p, const char *weights, int device, uint32_t nb, void *pool, size_t poolb);
+int px_ready(px *p);                          /* px.h:386-397: join the bring-up; 0 or -1 */
+int px_poll(px *p);                           /* px.h:399-402: 1 once the bring-up has finished */
+/* Replaces px_submit (px.h:405-418): n <= nb inputs (PX_IN halves each; adjacent ones in one copy) into slot
+ * buf < PX_NBUF; async H2D, forward graph, D2H into hout[buf]. */
+int px_submit(px *p, uint32_t buf, uint16_t *const *in, uint32_t n);
+int px_query(px *p, uint32_t buf);            /* px.h:420-423 */
+const float *px_wait(px *p, uint32_t buf);    /* px.h:425-428: scores [n][nt] or NULL */
+void px_close(px *p);                         /* px.h:455-492 */
+/* PixAI attention kernel alone: q8 / k8 / v8 [nseq][16][L][64] E4M3 (L = 576 or 5184) -> out [nseq L][1024] E4M3,
+ * the flash8<L> arithmetic of kern_common.cuh:403-543 (px_kernels.cu:140-154). */
+int xtb_px_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nseq, int L, uint8_t *out,
+                     float sinv, float vo, void *stream);
+/* extensions: resident forward (inputs uploaded with px_upload or written at px_input), scores / head vectors of
+ * the last forward, the engine's stream, launches per forward, per-kind kernel times of one direct forward */
+int px_forward_resident(px *p);
+int px_upload(px *p, uint16_t *const *in, uint32_t n);
+int px_download(px *p, float *out, uint32_t n);
+int px_head_input(px *p, uint16_t *o, uint32_t n);
+void *px_stream(px *p);
+void *px_input(px *p);
+int px_launches_per_forward(px *p);
+int px_profile(px *p, float *ms, int kinds);
+const char *px_prof_name(int k);
+
 #ifdef __cplusplus
 }
 #endif

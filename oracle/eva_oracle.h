@@ -67,6 +67,23 @@ void or_prune24(uint8_t *w, int n, int k, int wanda);
 
 int or_threads(void);
 
+/* PixAI tagger (px_oracle.c; src/engine/px.h + px_kernels.cu): window-major tokens, sequences of L tokens */
+void or_px_embed(const uint16_t *in, int rows, const uint16_t *pe, const float *pos, const float *w, const float *b,
+                 uint16_t *x);
+void or_px_qkv_epilogue(const float *acc, int rows, int L, const float *bias, const float *cs, float cq, float ck,
+                        float cv, uint8_t *q8, uint8_t *k8, uint8_t *v8);
+void or_px_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nseq, int L, float sinv, float vo,
+                     int key_tile, int slice_rows, uint8_t *out);
+void or_px_resid_bias(uint16_t *x, const float *acc, const float *bias, int rows);
+void or_px_fc1_epilogue(const float *acc, int rows, const float *b1, const float *rs, uint8_t *u8);
+void or_px_head(const uint16_t *x, int nimg, const float *w, const float *b, const float *U, const uint16_t *hpos,
+                const uint16_t *wv, const uint16_t *hw, const float *hb, int nt, float *scores, uint16_t *o_out);
+/* whole forward from a pixai.bin v3; in: nimg x [5184][592] fp16; scores [nimg][nt]; o_out (optional) the head's
+ * pooled-and-projected vectors [nimg][1024] fp16 */
+int or_px_forward(const char *model, const uint16_t *in, int nimg, int key_tile, int slice_rows, float *scores,
+                  uint16_t *o_out);
+int or_px_model_nt(const char *model);
+
 /* GPU preprocessing restated (prep_oracle.c; src/core/procimg.h's wd path) */
 uint32_t or_div255(uint32_t x);
 void or_over_white(uint8_t *img, int w, int h, int stride, int alpha);

@@ -58,6 +58,17 @@ def lib():
             "or_half": (None, [_u8, C.c_int, C.c_int, C.c_int, _u8, C.c_int]),
             "or_prep": (None, [_u8, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _u16]),
             "or_prep_level": (C.c_int, [C.c_int, C.c_int, C.c_int]),
+            "or_px_embed": (None, [_u16, C.c_int, _u16, _f32, _f32, _f32, _u16]),
+            "or_px_qkv_epilogue": (None, [_f32, C.c_int, C.c_int, _f32, _f32, C.c_float, C.c_float, C.c_float, _u8,
+                                          _u8, _u8]),
+            "or_px_attention": (None, [_u8, _u8, _u8, C.c_int, C.c_int, C.c_float, C.c_float, C.c_int, C.c_int,
+                                       _u8]),
+            "or_px_resid_bias": (None, [_u16, _f32, _f32, C.c_int]),
+            "or_px_fc1_epilogue": (None, [_f32, C.c_int, _f32, _f32, _u8]),
+            "or_px_head": (None, [_u16, C.c_int, _f32, _f32, _f32, _u16, _u16, _u16, _f32, C.c_int, _f32,
+                                  C.c_void_p]),
+            "or_px_forward": (C.c_int, [C.c_char_p, _u16, C.c_int, C.c_int, C.c_int, _f32, C.c_void_p]),
+            "or_px_model_nt": (C.c_int, [C.c_char_p]),
         }
         for name, (res, args) in sig.items():
             f = getattr(l, name)
@@ -113,3 +124,20 @@ def forward(model, inputs, key_tile=64, slice_rows=16, want_pn=False):
     if rc:
         raise RuntimeError("oracle forward failed")
     return (scores, pn) if want_pn else scores
+
+
+def px_forward(model, inputs, key_tile=64, slice_rows=16, want_o=False):
+    """PixAI scores [nimg][nt] (and the head's fp16 o [nimg][1024]) of the whole forward on the CPU; the defaults
+    are the reference's attention tiling."""
+    inputs = np.ascontiguousarray(inputs, np.uint16)
+    nimg = inputs.shape[0]
+    nt = lib().or_px_model_nt(model.encode())
+    if nt <= 0:
+        raise RuntimeError(f"oracle cannot read {model}")
+    scores = np.empty((nimg, nt), np.float32)
+    o = np.empty((nimg, 1024), np.uint16) if want_o else None
+    rc = lib().or_px_forward(model.encode(), inputs.ravel(), nimg, key_tile, slice_rows, scores,
+                             o.ctypes.data_as(C.c_void_p) if want_o else None)
+    if rc:
+        raise RuntimeError("oracle PixAI forward failed")
+    return (scores, o) if want_o else scores

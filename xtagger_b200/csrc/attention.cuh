@@ -1,4 +1,5 @@
-// FP8 flash attention on tcgen05 for the EVA02-L tagger: one CTA per (128-query tile, head, image), 1025 tokens.
+// FP8 flash attention on tcgen05 for the EVA02-L tagger (1025 tokens) and the PixAI tagger (sequences of 576 or
+// 5184 tokens, AttSeq below): one CTA per pair of 128-query tiles of one (sequence, head).
 // Replaces flash8<1025> (kern_common.cuh:403-543) with its arithmetic and decisions:
 //   - keys in tiles of 64, as the reference; scores are raw E4M3 dot products and sinv = 1 / (cq ck) folds the
 //     dequantisation (and the softmax scale times log2 e, which the weights carry in Wq) into the exp2 argument:
@@ -37,13 +38,29 @@ namespace xtb {
 constexpr float ATT_RESCALE = 8.0f;
 constexpr float ATT_PSKIP = 10.0f;
 constexpr int ATT_SUB = 64;                       // keys per softmax step (the reference's key tile)
-constexpr int ATT_NSUB = (T + ATT_SUB - 1) / ATT_SUB;  // 17 steps; the last holds 1 key
-constexpr int ATT_NK = (ATT_NSUB + 1) / 2;        // 9 K / V tiles of 128 keys
+constexpr int ATT_NSUB = (T + ATT_SUB - 1) / ATT_SUB;  // EVA02-L: 17 steps; the last holds 1 key
 constexpr int ATT_KS = 3;                         // K / V ring depth (128-key tiles)
 constexpr int ATT_G = 2;                          // query tiles (groups) per CTA
-constexpr int ATT_QTF = (T - 1) / 128;               // full query tiles (8): rows 0 .. 1023
-constexpr int ATT_QPAIRS = ATT_QTF / ATT_G;           // CTAs per (head, image); row 1024 goes to k_attention_last
+constexpr int ATT_QTF = (T - 1) / 128;               // EVA02-L: full query tiles (8): rows 0 .. 1023
 constexpr int ATT_THREADS = 64 + 32 * 4 * ATT_G;
+
+// Sequence shape of one attention instance: L tokens per (sequence, head), RS rows between consecutive
+// (sequence, head) blocks of q8 / k8 / v8, NQT query tiles of 128 rows. Tile i starts at row min(128 i, L - 128):
+// when L is not a multiple of 128 the last tile overlaps its neighbour and writes only its own rows; the rows it
+// shares are computed identically in both (the lazy-rescale and dead-tile decisions are per 16-row slice, and a
+// tile start is a multiple of 64). EVA02-L: <1025, 1152, 8> (rows 0 .. 1023; row 1024 by k_attention_last);
+// PixAI windows <576, 576, 5>, global blocks <5184, 5184, 41>.
+template <int L_, int RS_, int NQT_>
+struct AttSeq {
+    static constexpr int L = L_, RS = RS_, NQT = NQT_;
+    static constexpr int NSUB = (L + ATT_SUB - 1) / ATT_SUB;  // 64-key softmax steps
+    static constexpr int NK = (NSUB + 1) / 2;                 // K / V tiles of 128 keys
+    static constexpr int PAIRS = (NQT + ATT_G - 1) / ATT_G;   // CTAs per (sequence, head)
+    static constexpr bool RAGGED = (L % ATT_SUB) != 0;        // the last step holds fewer than 64 keys
+    __device__ __forceinline__ static int qstart(int i) { return min(i * 128, L - 128); }
+    static_assert(L >= 128 && NQT >= 1 && (NQT - 1) * 128 < L, "query tiles");
+};
+using AttEva = AttSeq<T, TP, ATT_QTF>;
 constexpr int ATT_Q_BYTES = 128 * 64;
 constexpr int ATT_K_BYTES = 128 * 64;
 constexpr int ATT_V_BYTES = 128 * 64;
@@ -124,10 +141,12 @@ __device__ __forceinline__ uint32_t e4m3x2_via_f16(float a, float b)
     return e4m3x2(f.x, f.y);
 }
 
+template <class SQ>
 __global__ void __launch_bounds__(ATT_THREADS, 2)
     k_attention(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                 const __grid_constant__ CUtensorMap tv, uint8_t *__restrict__ out, float sinv, float vo, uint32_t *err)
 {
+    constexpr int NSUB = SQ::NSUB, NK = SQ::NK, RS = SQ::RS, L = SQ::L;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sQ = smem;                                  // [ATT_G]
@@ -144,7 +163,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt0 = blockIdx.x * ATT_G, h = blockIdx.y, b = blockIdx.z;
-    constexpr int ng = ATT_G;                            // query tiles this CTA holds
+    const int ng = min(ATT_G, SQ::NQT - qt0);            // query tiles this CTA holds (CTA-uniform)
     const int bh = b * NH + h;
 
     if (threadIdx.x == 0) {
@@ -175,14 +194,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     if (warp == 0) {
         if (elect_one()) {
             mbar_arrive_expect_tx(q_full, ng * ATT_Q_BYTES);
-            for (int g = 0; g < ng; g++) tma_load_2d(sQ + g * ATT_Q_BYTES, &tq, q_full, 0, bh * TP + (qt0 + g) * 128);
+            for (int g = 0; g < ng; g++) tma_load_2d(sQ + g * ATT_Q_BYTES, &tq, q_full, 0, bh * RS + SQ::qstart(qt0 + g));
             uint32_t ph = 0;
             int st = 0;
-            for (int j = 0; j < ATT_NK; j++) {
+            for (int j = 0; j < NK; j++) {
                 if (!mbar_wait(&kv_empty[st], ph ^ 1, err, XTB_ERR_WAIT_ATTN)) break;
                 mbar_arrive_expect_tx(&kv_full[st], ATT_K_BYTES + ATT_V_BYTES);
-                tma_load_2d(sK + st * ATT_K_BYTES, &tk, &kv_full[st], 0, bh * TP + j * 128);
-                tma_load_2d(sV + st * ATT_V_BYTES, &tv, &kv_full[st], 0, bh * TP + j * 128);
+                tma_load_2d(sK + st * ATT_K_BYTES, &tk, &kv_full[st], 0, bh * RS + j * 128);
+                tma_load_2d(sV + st * ATT_V_BYTES, &tv, &kv_full[st], 0, bh * RS + j * 128);
                 if (++st == ATT_KS) {
                     st = 0;
                     ph ^= 1;
@@ -194,9 +213,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             // S: N = 64 keys. PV: A = P from TMEM (16 columns of the group's S buffer), B = V, MN-major (bit 16)
             constexpr uint32_t ID_S = idesc_m128(64), ID_PV = idesc_m128(64) | (1u << 16);
             bool ok = mbar_wait(q_full, 0, err, XTB_ERR_WAIT_ATTN);
-            for (int u = 0; u <= ATT_NSUB && ok; u++) {
+            for (int u = 0; u <= NSUB && ok; u++) {
                 const int j = u >> 1, st = j % ATT_KS;
-                if (u < ATT_NSUB && !(u & 1) && !(ok = mbar_wait(&kv_full[st], (j / ATT_KS) & 1, err, XTB_ERR_WAIT_ATTN)))
+                if (u < NSUB && !(u & 1) && !(ok = mbar_wait(&kv_full[st], (j / ATT_KS) & 1, err, XTB_ERR_WAIT_ATTN)))
                     break;
                 const int w = u - 1, wst = (w >> 1) % ATT_KS;
                 for (int g = 0; g < ng && ok; g++) {
@@ -211,7 +230,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                                         (w > 0 || kk > 0));
                         umma_commit(&pv_done[g]);
                     }
-                    if (u < ATT_NSUB) {  // S_g,u = Q_g K_u^T, issued after PV_g,w (the tensor core keeps the order)
+                    if (u < NSUB) {  // S_g,u = Q_g K_u^T, issued after PV_g,w (the tensor core keeps the order)
                         const uint32_t q0 = smem_u32(sQ + g * ATT_Q_BYTES);
                         const uint32_t k0 = smem_u32(sK + st * ATT_K_BYTES) + (u & 1) * 4096;
 #pragma unroll
@@ -221,10 +240,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                     }
                 }
                 if (!ok) break;
-                if (u > 0 && ((w & 1) || w == ATT_NSUB - 1)) umma_commit(&kv_empty[wst]);  // the K / V tile is used up
+                if (u > 0 && ((w & 1) || w == NSUB - 1)) umma_commit(&kv_empty[wst]);  // the K / V tile is used up
             }
         }
-    } else {
+    } else if ((warp - 2) / 4 < ng) {
         const int g = (warp - 2) / 4;                    // query tile (group) of this warp
         const int quad = warp & 3;
         const int r = quad * 32 + lane;                  // query row within the tile = TMEM lane
@@ -235,15 +254,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         const float2 sv2 = make_float2(sinv, sinv);
         float m = -1e30f, l = 0.f;
         bool ok = true;
-        for (int u = 0; u < ATT_NSUB && ok; u++) {
-            const int nvalid = min(ATT_SUB, T - u * ATT_SUB);
+        for (int u = 0; u < NSUB && ok; u++) {
+            const int nvalid = min(ATT_SUB, L - u * ATT_SUB);
             // S_g,u has landed, and with it every earlier MMA of the CTA (PV_g,u-1 included)
             if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[g], u & 1, err, XTB_ERR_WAIT_ATTN)))) break;
             tc_fence_after();
             uint32_t pw[16];
             // one pass with the running max: tile max, p = exp2(s sinv - m sinv), l_tile, P
             float tm = -INFINITY, lt = 0.f;
-            const bool full = u < ATT_NSUB - 1;          // the last step holds one key
+            const bool full = !SQ::RAGGED || u < NSUB - 1;  // EVA02-L: the last step holds one key
             if (u == 0) tm = tile_max(sS);
             else if (full) exp_pass<true>(sS, pw, nvalid, sv2, m, &tm, &lt);
             else exp_pass<false>(sS, pw, nvalid, sv2, m, &tm, &lt);
@@ -287,7 +306,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[g]);
         }
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[g], (ATT_NSUB - 1) & 1, err, XTB_ERR_WAIT_ATTN));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[g], (NSUB - 1) & 1, err, XTB_ERR_WAIT_ATTN));
         if (ok) {
             tc_fence_after();
             const float f = vo / l;
@@ -301,10 +320,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
                 for (int i = 0; i < 32; i += 4)
                     w[c * 8 + (i >> 2)] = e4m3x2_via_f16(v[i] * f, v[i + 1] * f) | (e4m3x2_via_f16(v[i + 2] * f, v[i + 3] * f) << 16);
             }
-            const int t = (qt0 + g) * 128 + r;
-            uint4 *o = (uint4 *)(out + ((size_t)b * T + t) * D + h * HD);
+            const int t = SQ::qstart(qt0 + g) + r;
+            if (t >= (qt0 + g) * 128) {  // rows shared with the previous tile are written by that tile
+                uint4 *o = (uint4 *)(out + ((size_t)b * L + t) * D + h * HD);
 #pragma unroll
-            for (int c = 0; c < 4; c++) o[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                for (int c = 0; c < 4; c++) o[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+            }
         }
     }
     __syncthreads();

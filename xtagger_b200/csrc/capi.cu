@@ -70,6 +70,14 @@ int xtb_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int n
     return launch_attention(a, nimg, out, sinv, vo, S(stream));
 }
 
+int xtb_px_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nseq, int L, uint8_t *out,
+                     float sinv, float vo, void *stream)
+{
+    Attn a;
+    if (nseq <= 0 || (L != PXLW && L != PXT) || make_attn_rows(&a, q8, k8, v8, nseq * L)) return -1;
+    return launch_px_attention(a, nseq, L, out, sinv, vo, S(stream));
+}
+
 int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, void *stream)
 {
     Operand A;

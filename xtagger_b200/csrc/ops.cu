@@ -8,6 +8,7 @@
 #include "gemm_sp.cuh"
 #include "host.h"
 #include "ops.h"
+#include "pixai.cuh"
 #include "rowops.cuh"
 
 namespace xtb {
@@ -225,9 +226,9 @@ int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, 
 
 int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st)
 {
-    if (set_smem((const void *)k_attention, ATT_SMEM)) return -1;
-    dim3 grid(ATT_QPAIRS, NH, nimg);
-    k_attention<<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
+    if (set_smem((const void *)k_attention<AttEva>, ATT_SMEM)) return -1;
+    dim3 grid(AttEva::PAIRS, NH, nimg);
+    k_attention<AttEva><<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
     XTB_CK(cudaGetLastError());
     k_attention_last<<<nimg * NH, ATT_LAST_THREADS, 0, st>>>(a.q8, a.k8, a.v8, out, sinv, vo);
     XTB_CK(cudaGetLastError());
@@ -452,7 +453,121 @@ int prepare_kernels()
     for (const void *k : sp)
         if (set_smem(k, SpCfg::SMEM)) return -1;
     if (set_smem((const void *)k_ln_e4m3, LN_SMEM)) return -1;
-    return set_smem((const void *)k_attention, ATT_SMEM);
+    if (set_smem((const void *)k_attention<AttEva>, ATT_SMEM)) return -1;
+    return 0;
+}
+
+// ---- PixAI ----
+using AttPxW = AttSeq<PX_LW, PX_LW, (PX_LW + 127) / 128>;
+using AttPxG = AttSeq<PX_T, PX_T, (PX_T + 127) / 128>;
+
+int launch_px_patch(const Operand &in, const Operand &pe, int rows, __half *x, cudaStream_t st)
+{
+    EpiPxPatch::Params p{x, rows};
+    return run_gemm<EpiPxPatch, 256, true, false, false>(in, pe, rows, D, nullptr, 0, 1, 1.0f, p, st);
+}
+
+int launch_px_embed(__half *x, const float *pos, const float *w, const float *b, int rows, cudaStream_t st)
+{
+    k_px_embed<<<(rows + 7) / 8, 256, 0, st>>>(x, pos, w, b, rows);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
+int launch_px_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, int L, uint8_t *q8, uint8_t *k8,
+                  uint8_t *v8, const float *cs, const float *bias, float cq, float ck, float cv, cudaStream_t st)
+{
+    if (w.uniform <= 0.0f || (L != PX_LW && L != PX_T) || rows % L) {
+        fprintf(stderr, "eva: px qkv: per-tensor weights and whole sequences of 576 or 5184 rows expected\n");
+        return -1;
+    }
+    EpiPxQKV::Params p{q8, k8, v8, (const float2 *)cs, bias, cq, ck, cv, rows, L};
+    return run_proj<EpiPxQKV, W_QKV>(h, w, rows, ascale, p, st);
+}
+
+int make_attn_rows(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int rows)
+{
+    const uint64_t r = (uint64_t)rows * NH;
+    a->q8 = q8;
+    a->k8 = k8;
+    a->v8 = v8;
+    if (make_tmap_2d(&a->tq, q8, HD, r, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
+    if (make_tmap_2d(&a->tk, k8, HD, r, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
+    if (make_tmap_2d(&a->tv, v8, HD, r, HD, HD, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
+    return 0;
+}
+
+template <class SQ>
+static int run_attention_seq(const Attn &a, int nseq, uint8_t *out, float sinv, float vo, cudaStream_t st)
+{
+    auto kern = k_attention<SQ>;
+    if (set_smem((const void *)kern, ATT_SMEM)) return -1;
+    dim3 grid(SQ::PAIRS, NH, nseq);
+    kern<<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
+int launch_px_attention(const Attn &a, int nseq, int L, uint8_t *out, float sinv, float vo, cudaStream_t st)
+{
+    if (L == PX_LW) return run_attention_seq<AttPxW>(a, nseq, out, sinv, vo, st);
+    if (L == PX_T) return run_attention_seq<AttPxG>(a, nseq, out, sinv, vo, st);
+    fprintf(stderr, "eva: px attention: sequence length %d (576 or 5184)\n", L);
+    return -1;
+}
+
+int launch_px_resid(const Operand &a, const Weight8 &w, float ascale, int rows, const CUtensorMap &xm,
+                    const float *bias, WeightUse use, cudaStream_t st)
+{
+    if (w.uniform <= 0.0f) return -1;
+    EpiPxResid::Params p{bias, rows};
+    if (use == W_O) return run_proj<EpiPxResid, W_O>(a, w, rows, ascale, p, st, &xm);
+    if (use == W_FC2) return run_proj<EpiPxResid, W_FC2>(a, w, rows, ascale, p, st, &xm);
+    return -1;
+}
+
+int px_u8_map(CUtensorMap *m, uint8_t *u8, int rows)
+{
+    return make_tmap_2d(m, u8, PX_HID, (uint64_t)rows, PX_HID, 128, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int launch_px_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, const CUtensorMap &um, const float *b1,
+                  const float *rs, cudaStream_t st)
+{
+    if (w.uniform <= 0.0f) return -1;
+    EpiPxFC1::Params p{b1, rs, rows};
+    return run_proj<EpiPxFC1, W_FC1>(h, w, rows, ascale, p, st, &um);
+}
+
+int launch_px_head(const __half *x, int nimg, const float *w, const float *b, const __half *hpos, const float *U,
+                   const __half *wv, __half *y, float *s, __half *P, float *part, __half *o, cudaStream_t st)
+{
+    if (set_smem((const void *)k_px_head_ln_score, PX_HEAD_SMEM)) return -1;
+    const int rows = nimg * PX_T;
+    int grid = 3 * num_sms(current_device());
+    if (grid > (rows + 7) / 8) grid = (rows + 7) / 8;
+    k_px_head_ln_score<<<grid, 256, PX_HEAD_SMEM, st>>>(x, w, b, hpos, U, y, s, rows);
+    XTB_CK(cudaGetLastError());
+    k_px_head_softmax<<<nimg * NH, 256, 0, st>>>(s, P);
+    XTB_CK(cudaGetLastError());
+    k_px_head_pool<<<dim3(nimg, PX_NCH), 512, 0, st>>>(P, y, part);
+    XTB_CK(cudaGetLastError());
+    k_px_head_v<<<nimg * NH, 256, 0, st>>>(part, wv, o);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
+// Shared-memory opt-in of the PixAI kernels (before a stream capture).
+int prepare_px_kernels()
+{
+    if (prepare_kernels()) return -1;
+    if (set_smem((const void *)k_gemm<EpiPxPatch, 256, true, false, false>, GemmCfg<256>::SMEM)) return -1;
+    if (prepare_proj<EpiPxQKV, W_QKV>() || prepare_proj<EpiPxResid, W_O>() || prepare_proj<EpiPxFC1, W_FC1>() ||
+        prepare_proj<EpiPxResid, W_FC2>())
+        return -1;
+    if (set_smem((const void *)k_attention<AttPxW>, ATT_SMEM) || set_smem((const void *)k_attention<AttPxG>, ATT_SMEM))
+        return -1;
+    return set_smem((const void *)k_px_head_ln_score, PX_HEAD_SMEM);
 }
 
 }  // namespace xtb

@@ -100,6 +100,28 @@ int launch_fc1_sp(const Operand &h, const SparseW &w, float ascale, int rows, ui
 int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
                   const float *d, cudaStream_t st);
 
+// ---- PixAI tagger (pixai.cuh; ViTDet-L at 1008^2, window-major tokens) ----
+constexpr int PXT = 5184, PXLW = 576, PXHID = 4736;
+int launch_px_patch(const Operand &in, const Operand &pe, int rows, __half *x, cudaStream_t st);
+int launch_px_embed(__half *x, const float *pos, const float *w, const float *b, int rows, cudaStream_t st);
+int launch_px_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, int L, uint8_t *q8, uint8_t *k8,
+                  uint8_t *v8, const float *cs, const float *bias, float cq, float ck, float cv, cudaStream_t st);
+// q8 / k8 / v8 [rows / L][16][L][64] for both sequence lengths: one set of tensor maps over rows * 16 rows of 64
+int make_attn_rows(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int rows);
+// L = 576 (windows) or 5184 (global): nseq sequences of L tokens -> out [nseq L][1024] E4M3
+int launch_px_attention(const Attn &a, int nseq, int L, uint8_t *out, float sinv, float vo, cudaStream_t st);
+// x (fp16 [rows][1024], as the TMA target xm) += alpha a W^T + bias
+int launch_px_resid(const Operand &a, const Weight8 &w, float ascale, int rows, const CUtensorMap &xm,
+                    const float *bias, WeightUse use, cudaStream_t st);
+// u8 [rows][4736] = E4M3(rs * gelu(alpha h W1^T + b1)); um: its tensor map (128-byte x 32-row boxes)
+int launch_px_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, const CUtensorMap &um, const float *b1,
+                  const float *rs, cudaStream_t st);
+int px_u8_map(CUtensorMap *m, uint8_t *u8, int rows);
+// attention-pool head: y, s, P, part scratch; o [nimg][1024] fp16
+int prepare_px_kernels();
+int launch_px_head(const __half *x, int nimg, const float *w, const float *b, const __half *hpos, const float *U,
+                   const __half *wv, __half *y, float *s, __half *P, float *part, __half *o, cudaStream_t st);
+
 // Per-column max |x| of an fp16 [rows][K] tensor folded into amax (fp32, K a multiple of 8).
 int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t st);
 

@@ -25,10 +25,42 @@ class Eva(C.Structure):
     ]
 
 
+PX_NB, PX_NBUF, PX_T = 4, 4, 5184
+PX_IN = PX_T * EVA_K0P
+
+
+class Px(C.Structure):
+    """Mirror of `struct px` in include/xtagger_b200.h."""
+    _fields_ = [
+        ("nt", C.c_uint32), ("ntp", C.c_uint32), ("nb", C.c_uint32),
+        ("hout", C.POINTER(C.c_float) * PX_NBUF),
+        ("impl", C.c_void_p),
+    ]
+
+
 _lib = None
 
 _P = C.c_void_p
+_PX = C.POINTER(Px)
 _SIGS = {
+    "px_open": (C.c_int, [_PX, C.c_char_p, C.c_int, _P, C.c_size_t]),
+    "px_open_ex": (C.c_int, [_PX, C.c_char_p, C.c_int, C.c_uint32, _P, C.c_size_t]),
+    "px_ready": (C.c_int, [_PX]),
+    "px_poll": (C.c_int, [_PX]),
+    "px_submit": (C.c_int, [_PX, C.c_uint32, C.POINTER(_P), C.c_uint32]),
+    "px_query": (C.c_int, [_PX, C.c_uint32]),
+    "px_wait": (C.POINTER(C.c_float), [_PX, C.c_uint32]),
+    "px_close": (None, [_PX]),
+    "px_forward_resident": (C.c_int, [_PX]),
+    "px_upload": (C.c_int, [_PX, C.POINTER(_P), C.c_uint32]),
+    "px_download": (C.c_int, [_PX, _P, C.c_uint32]),
+    "px_head_input": (C.c_int, [_PX, _P, C.c_uint32]),
+    "px_stream": (_P, [_PX]),
+    "px_input": (_P, [_PX]),
+    "px_launches_per_forward": (C.c_int, [_PX]),
+    "px_profile": (C.c_int, [_PX, _P, C.c_int]),
+    "px_prof_name": (C.c_char_p, [C.c_int]),
+    "xtb_px_attention": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, C.c_float, C.c_float, _P]),
     "eva_open": (C.c_int, [C.POINTER(Eva), C.c_char_p, C.c_int, _P, C.c_size_t, C.c_uint32]),
     "eva_open_ex": (C.c_int, [C.POINTER(Eva), C.c_char_p, C.POINTER(C.c_int), C.c_int, C.c_uint32, _P, C.c_size_t,
                               C.c_uint32]),
@@ -85,7 +117,7 @@ def header_symbols():
     """Names of every function declared in include/xtagger_b200.h."""
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b((?:eva|xtb)_[a-z0-9_]+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b((?:eva|xtb|px)_[a-z0-9_]+)\s*\(", src)))
 
 
 def lib():
