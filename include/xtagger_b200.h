@@ -256,6 +256,10 @@ void px_close(px *p);                         /* px.h:455-492 */
  * the flash8<L> arithmetic of kern_common.cuh:403-543 (px_kernels.cu:140-154). */
 int xtb_px_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nseq, int L, uint8_t *out,
                      float sinv, float vo, void *stream);
+/* PixAI fc1 GEMM alone: u8 [rows][4736] = E4M3(rs * gelu(ascale wscale h W1^T + b1)), h E4M3 [rows][1024], W1 E4M3
+ * [4736][1024] with one scale per tensor (k_pfc1, px_kernels.cu:203-239). */
+int xtb_px_fc1(const uint8_t *h, int rows, const uint8_t *w1, float wscale, float ascale, const float *b1,
+               const float *rs, uint8_t *u8, void *stream);
 /* extensions: resident forward (inputs uploaded with px_upload or written at px_input), scores / head vectors of
  * the last forward, the engine's stream, launches per forward, per-kind kernel times of one direct forward */
 int px_forward_resident(px *p);

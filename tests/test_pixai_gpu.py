@@ -53,13 +53,18 @@ def test_px_engine_matches_oracle(xlib, cuda, O, px_model):
         assert eng.launches_per_forward() == 2 + 7 * 2 + 5
     finally:
         eng.close()
-    want, wo = O.px_forward(px_model, x, want_o=True)            # the reference's attention tiling
-    alt = O.px_forward(px_model, x, key_tile=128, slice_rows=1)  # another tiling of the same arithmetic
+    want, wo = O.px_forward(px_model, x, want_o=True)                           # the reference's attention tiling
+    alt, ao = O.px_forward(px_model, x, key_tile=128, slice_rows=1, want_o=True)  # another tiling, same arithmetic
     floor = float(np.abs(alt - want).max())
     err = float(np.abs(got - want).max())
     assert np.isfinite(got).all()
     assert err <= max(2e-3, 1.5 * floor), f"scores: max |diff| {err:.3e} (oracle tiling noise floor {floor:.3e})"
-    G.assert_f16_close(o, wo, 2e-2, "head vector o")
+    # the head vector: FP8 rounding flips inside the forward move it by about as much as another attention tiling
+    g, w, a = G.f16(o), G.f16(wo), G.f16(ao)
+    scale = float(np.abs(w).max())
+    err_o, floor_o = float(np.abs(g - w).max()), float(np.abs(a - w).max())
+    assert err_o <= max(2e-3 * scale, 2.0 * floor_o), f"o: max |diff| {err_o:.3e}, tiling floor {floor_o:.3e}"
+    assert np.corrcoef(g.ravel(), w.ravel())[0, 1] > 0.9999
 
 
 def test_px_engine_submit_slots(xlib, cuda, px_model):
@@ -78,3 +83,25 @@ def test_px_engine_submit_slots(xlib, cuda, px_model):
         assert np.array_equal(part[0], first[1])
     finally:
         eng.close()
+
+
+def test_px_fc1_gelu(xlib, cuda, O):
+    """fc1 GEMM + bias + exact-erf GELU + rs -> E4M3 against the oracle (libm erff): codes equal or one step apart
+    (a product on a rounding boundary), at least 99 % identical."""
+    import torch
+    rng = np.random.default_rng(44)
+    rows = 1000                                   # a partial last row tile
+    h = O.e4m3(rng.standard_normal((rows, 1024), dtype=np.float32) * 60)
+    w = O.e4m3(rng.standard_normal((4736, 1024), dtype=np.float32) * 100)
+    wscale, ascale = 0.02 / 100, 1.0 / 60
+    b1 = (rng.standard_normal(4736) * 0.5).astype(np.float32)
+    rs = (40 + 20 * rng.random(4736)).astype(np.float32)
+    acc = np.empty((rows, 4736), np.float32)
+    O.lib().or_gemm_e4m3(h, rows, 1024, w, 4736, np.ones((37, 8), np.float32), np.float32(wscale) * np.float32(ascale), acc)
+    want = np.empty((rows, 4736), np.uint8)
+    O.lib().or_px_fc1_epilogue(acc, rows, b1, rs, want)
+    out = G.zeros((rows, 4736), torch.uint8)
+    assert xlib.xtb_px_fc1(G.P(G.dev(h)), rows, G.P(G.dev(w)), wscale, ascale, G.P(G.dev(b1)), G.P(G.dev(rs)),
+                           G.P(out), None) == 0
+    G.check_error_word(xlib)
+    G.assert_e4m3_close(G.host(out), want, 1, 0.99, "px fc1")

@@ -78,6 +78,22 @@ int xtb_px_attention(const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, in
     return launch_px_attention(a, nseq, L, out, sinv, vo, S(stream));
 }
 
+int xtb_px_fc1(const uint8_t *h, int rows, const uint8_t *w1, float wscale, float ascale, const float *b1,
+               const float *rs, uint8_t *u8, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    CUtensorMap um;
+    if (!rows_ok(rows, "xtb_px_fc1") || !(wscale > 0.0f) || make_operand(&A, h, rows, D, 128) ||
+        make_operand(&W.op, w1, PXHID, D, weight_box_rows(W_FC1)) || px_u8_map(&um, u8, rows))
+        return -1;
+    W.ws = nullptr;
+    W.n = PXHID;
+    W.k = D;
+    W.uniform = wscale;
+    return launch_px_fc1(A, W, ascale, rows, um, b1, rs, S(stream));
+}
+
 int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, void *stream)
 {
     Operand A;

@@ -11,6 +11,7 @@
 // Tokens are window-major throughout (9 windows of 576); windowed blocks attend within 576-token sequences, global
 // blocks over all 5184 tokens of an image.
 #pragma once
+#include "attention.cuh"
 #include "epilogues.cuh"
 #include "ops.h"
 
@@ -187,6 +188,33 @@ struct EpiPxResid {
     }
 };
 
+// Exact-erf GELU, v (1 + erf(v / sqrt 2)) / 2, with erf from Abramowitz & Stegun 7.1.26 (Handbook of Mathematical
+// Functions, 1964): erf(x) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-x^2), t = 1 / (1 + p x), x >= 0,
+// absolute error below 1.5e-7. With hq = (1 - erf(|z|)) / 2 (the coefficients carry the 1/2), z = v / sqrt 2:
+// gelu = v - v hq for v >= 0 and v hq for v < 0, so the small tail is computed without cancellation. The result
+// feeds an E4M3 code (3 mantissa bits), so this matches the reference's erff-based value except where the two sit
+// within ~1e-7 of a rounding boundary. Two elements at a time on packed f32x2 operations; two MUFU operations (rcp,
+// ex2) per element.
+__device__ __forceinline__ float2 gelu_erf2(float2 v)
+{
+    constexpr float P = 0.3275911f, A1 = 0.5f * 0.254829592f, A2 = 0.5f * -0.284496736f, A3 = 0.5f * 1.421413741f,
+                    A4 = 0.5f * -1.453152027f, A5 = 0.5f * 1.061405429f;
+    const float2 az = mul2(make_float2(fabsf(v.x), fabsf(v.y)), make_float2(0.70710678f, 0.70710678f));
+    const float2 d = fma2(az, make_float2(P, P), make_float2(1.0f, 1.0f));
+    float2 t;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.y) : "f"(d.y));
+    float2 poly = fma2(t, make_float2(A5, A5), make_float2(A4, A4));
+    poly = fma2(t, poly, make_float2(A3, A3));
+    poly = fma2(t, poly, make_float2(A2, A2));
+    poly = fma2(t, poly, make_float2(A1, A1));
+    poly = mul2(t, poly);
+    const float2 arg = mul2(mul2(az, make_float2(-1.44269504f, -1.44269504f)), az);
+    const float2 e = make_float2(ex2(arg.x), ex2(arg.y));
+    const float2 g = mul2(v, mul2(poly, e));   // v hq
+    return make_float2(v.x >= 0.0f ? v.x - g.x : g.x, v.y >= 0.0f ? v.y - g.y : g.y);
+}
+
 // ---- fc1 + GELU: u8 = E4M3(rs * gelu(acc + b1)), gelu(v) = v (1 + erf(v / sqrt 2)) / 2 ----
 // The warp's 32 rows x 128 units leave through one TMA store (128-byte rows, 128B swizzle: the staging layout).
 struct EpiPxFC1 {
@@ -210,10 +238,9 @@ struct EpiPxFC1 {
             for (int e = 0; e < 4; e++) {
                 const float4 b4 = __ldg(b4p + 4 * c + e), r4 = __ldg(r4p + 4 * c + e);
                 const float *a = acc + 16 * c + 4 * e;
-                float v[4] = {a[0] + b4.x, a[1] + b4.y, a[2] + b4.z, a[3] + b4.w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) v[k] *= 0.5f * (1.0f + erff(v[k] * 0.70710678f));
-                w[e] = e4m3x2(v[0] * r4.x, v[1] * r4.y) | (e4m3x2(v[2] * r4.z, v[3] * r4.w) << 16);
+                const float2 g0 = mul2(gelu_erf2(add2(make_float2(a[0], a[1]), make_float2(b4.x, b4.y))), make_float2(r4.x, r4.y));
+                const float2 g1 = mul2(gelu_erf2(add2(make_float2(a[2], a[3]), make_float2(b4.z, b4.w))), make_float2(r4.z, r4.w));
+                w[e] = e4m3x2(g0.x, g0.y) | (e4m3x2(g1.x, g1.y) << 16);
             }
             *(uint4 *)stage_chunk(cx.stage, cx.lane, c) = make_uint4(w[0], w[1], w[2], w[3]);
         }

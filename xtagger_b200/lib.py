@@ -61,6 +61,7 @@ _SIGS = {
     "px_profile": (C.c_int, [_PX, _P, C.c_int]),
     "px_prof_name": (C.c_char_p, [C.c_int]),
     "xtb_px_attention": (C.c_int, [_P, _P, _P, C.c_int, C.c_int, _P, C.c_float, C.c_float, _P]),
+    "xtb_px_fc1": (C.c_int, [_P, C.c_int, _P, C.c_float, C.c_float, _P, _P, _P, _P]),
     "eva_open": (C.c_int, [C.POINTER(Eva), C.c_char_p, C.c_int, _P, C.c_size_t, C.c_uint32]),
     "eva_open_ex": (C.c_int, [C.POINTER(Eva), C.c_char_p, C.POINTER(C.c_int), C.c_int, C.c_uint32, _P, C.c_size_t,
                               C.c_uint32]),
