@@ -59,12 +59,16 @@ def main():
     for _ in range(a.warmup):
         eng.forward_resident()
     torch.cuda.synchronize()
+    from xtagger_b200.clocks import Clocks
+    clk = Clocks(torch.cuda.current_device())
+    clk.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for _ in range(a.steps):
         eng.forward_resident()
     e1.record(st)
     torch.cuda.synchronize()
+    clocks = clk.stop()
     t = e0.elapsed_time(e1) / 1e3
     value = a.batch * a.steps / t
     inputs = [pool[i] for i in range(a.batch)]
@@ -92,7 +96,7 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "fc1 (tcgen05 E4M3 GEMM + bias / GELU epilogue)",
                          "achieved": achieved, "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk,
                          "peak_source": src, "launch_ms": fc1_ms},
-            "profile_ms": prof, "gpu_launches_per_forward": launches}
+            "profile_ms": prof, "gpu_launches_per_forward": launches, "clocks": clocks}
     if a.cpu:
         from oracle import oracle as O
         x = pool[:1]

@@ -59,6 +59,19 @@ struct StagingOf<E, decltype((void)E::STAGING_PER_WARP)> {
     static constexpr int v = E::STAGING_PER_WARP;
 };
 
+// Streaming epilogues (Epi::STREAM, per-tensor weights only): the accumulator is handed over 32 columns at a time,
+// apply_chunk(params, raw[32], scale, chunk, ctx, state), as soon as each chunk's TMEM load has landed, with the
+// next chunk's load already in flight; finish(params, ctx, state) after the last chunk. No COLS-wide register copy
+// of the accumulator, and the TMEM load latency hides behind the previous chunk's math.
+template <class E, class = void>
+struct StreamOf {
+    static constexpr bool v = false;
+};
+template <class E>
+struct StreamOf<E, decltype((void)E::STREAM)> {
+    static constexpr bool v = E::STREAM;
+};
+
 // Epilogue context of one thread: output row row0 + lane, columns col0 .. col0 + COLS - 1.
 struct EpiCtx {
     int row0;        // first row of this warp's 32 rows
@@ -210,6 +223,35 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
             cx.col0 = nb * BN + half * COLS;
             typename Epi::State es;
             Epi::begin(ep, cx, es);  // per-tile loads issued before the accumulator is ready
+            if constexpr (!PROMOTE && StreamOf<Epi>::v) {
+                static_assert(COLS % 32 == 0, "streaming epilogues take 32-column chunks");
+                const float s = g.ascale * Epi::col_scale(ep, cx) * g.wsu;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
+                tc_fence_after();
+                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * BN + half * COLS;
+                float v[2][32];
+                tmem_ld16(taddr, v[0]);
+                tmem_ld16(taddr + 16, v[0] + 16);
+#pragma unroll
+                for (int c = 0; c < COLS / 32; c++) {
+                    tmem_wait_ld_regs(v[c & 1]);
+                    if (c + 1 < COLS / 32) {
+                        tmem_ld16(taddr + 32 * (c + 1), v[(c + 1) & 1]);
+                        tmem_ld16(taddr + 32 * (c + 1) + 16, v[(c + 1) & 1] + 16);
+                    } else {  // every chunk is in registers: the buffer goes back to the MMA warp
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[tb]);
+                    }
+                    Epi::apply_chunk(ep, v[c & 1], s, c, cx, es);
+                }
+                if (++tb == TBUF) {
+                    tb = 0;
+                    tph ^= 1;
+                }
+                Epi::finish(ep, cx, es);
+                continue;
+            }
             float2 acc[COLS / 2];
 #pragma unroll
             for (int j = 0; j < COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);

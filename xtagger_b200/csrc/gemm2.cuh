@@ -178,6 +178,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN, GROUPS
             cx.col0 = nb * C::BN + (GROUPS ? 0 : half * COLS);
             typename Epi::State es;
             Epi::begin(ep, cx, es);  // per-tile loads issued before the accumulator is ready
+            if constexpr (!PROMOTE && !GROUPS && StreamOf<Epi>::v) {  // streaming epilogue (gemm.cuh)
+                static_assert(COLS % 32 == 0, "streaming epilogues take 32-column chunks");
+                const float s = g.ascale * Epi::col_scale(ep, cx) * g.wsu;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[tb], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
+                tc_fence_after();
+                const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + tb * C::BN + half * COLS;
+                float v[2][32];
+                tmem_ld16(taddr, v[0]);
+                tmem_ld16(taddr + 16, v[0] + 16);
+#pragma unroll
+                for (int c = 0; c < COLS / 32; c++) {
+                    tmem_wait_ld_regs(v[c & 1]);
+                    if (c + 1 < COLS / 32) {
+                        tmem_ld16(taddr + 32 * (c + 1), v[(c + 1) & 1]);
+                        tmem_ld16(taddr + 32 * (c + 1) + 16, v[(c + 1) & 1] + 16);
+                    } else {  // the whole buffer is in registers: hand it back to the MMA
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(tempty0 + tb * 8);
+                    }
+                    Epi::apply_chunk(ep, v[c & 1], s, c, cx, es);
+                }
+                if (++tb == TBUF) {
+                    tb = 0;
+                    tph ^= 1;
+                }
+                Epi::finish(ep, cx, es);
+                continue;
+            }
             float2 acc[COLS / 2];
 #pragma unroll
             for (int j = 0; j < COLS / 2; j++) acc[j] = make_float2(0.f, 0.f);

@@ -65,7 +65,7 @@ struct EpiPxQKV {
         int M, L;
     };
     using State = NoState;
-    static constexpr int STAGING_PER_WARP = 8192;  // both halves of the angles (4 KB each), then the output rows
+    static constexpr int STAGING_PER_WARP = 8192;  // both halves of the angles (4 KB each)
     __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     // The angles of the warp's 32 rows, half a row (16 pairs) at a time into 4 KB: consecutive rows are consecutive
     // table rows (wrapping at L), so each load instruction covers 4 whole 128-byte lines.
@@ -90,82 +90,61 @@ struct EpiPxQKV {
             stage_angles(p, cx, 1);
         }
     }
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
+    // A streaming epilogue: chunk c (32 columns) is dims 32 (c & 1) .. + 31 of head head0 + (c >> 1); its 32 E4M3
+    // bytes go straight to the row's 64-byte line of q8 / k8 / v8 (consecutive lanes are consecutive tokens, so a
+    // warp's stores cover whole lines of one head), and the angle rows stay staged for every chunk.
+    static constexpr bool STREAM = true;
+    __device__ __forceinline__ static void apply_chunk(const Params &p, const float *v, float s, int c,
+                                                       const EpiCtx &cx, State &)
     {
         const int which = cx.col0 >> 10;           // 0 q, 1 k, 2 v (a thread's 128 columns never straddle)
-        const int head0 = (cx.col0 & 1023) >> 6;   // two heads per thread
+        const int hh = c >> 1, h = c & 1;          // head within the thread's two, half of its 64 dims
+        const int n0 = hh * 64 + 32 * h;           // first column of the chunk within the thread's 128
         const float sc = which == 0 ? p.cq : which == 1 ? p.ck : p.cv;
-        const float2 sc2 = make_float2(sc, sc);
-        const float4 *bq = (const float4 *)(p.bias + cx.col0);
-        uint4 o[2][4];                             // E4M3 output: head hh, dims 16 q .. 16 q + 15
+        const float2 s2 = make_float2(s, s), sc2 = make_float2(sc, sc);
+        const float4 *bq = (const float4 *)(p.bias + cx.col0 + n0);
+        uint32_t w[8];
         if (which == 2) {
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++)
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const float *a = acc + hh * 64 + 16 * q;
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float4 b4 = __ldg(bq + hh * 16 + 4 * q + e);
-                        const float2 f0 = mul2(add2(make_float2(a[4 * e], a[4 * e + 1]), make_float2(b4.x, b4.y)), sc2);
-                        const float2 f1 = mul2(add2(make_float2(a[4 * e + 2], a[4 * e + 3]), make_float2(b4.z, b4.w)), sc2);
-                        w[e] = e4m3x2(f0.x, f0.y) | (e4m3x2(f1.x, f1.y) << 16);
-                    }
-                    o[hh][q] = make_uint4(w[0], w[1], w[2], w[3]);
-                }
+            for (int e = 0; e < 8; e++) {
+                const float4 b4 = __ldg(bq + e);
+                const float2 f0 = mul2(fma2(make_float2(v[4 * e], v[4 * e + 1]), s2, make_float2(b4.x, b4.y)), sc2);
+                const float2 f1 = mul2(fma2(make_float2(v[4 * e + 2], v[4 * e + 3]), s2, make_float2(b4.z, b4.w)), sc2);
+                w[e] = e4m3x2(f0.x, f0.y) | (e4m3x2(f1.x, f1.y) << 16);
+            }
         } else {
-            __syncwarp();
 #pragma unroll
-            for (int h = 0; h < 2; h++) {          // pairs 16 h .. 16 h + 15 (staged by begin)
+            for (int e = 0; e < 8; e++) {           // pairs 16 h + 2 e, 16 h + 2 e + 1 (dims 4 e .. 4 e + 3)
+                const float4 b4 = __ldg(bq + e);
+                const float4 a = *(const float4 *)stage_chunk(cx.stage + h * 4096, cx.lane, e);  // (cos, sin) x 2
+                float2 f[2];
 #pragma unroll
-                for (int q2 = 0; q2 < 2; q2++) {   // 8 pairs (16 dims of each head) per step
-                    float4 a[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) a[e] = *(const float4 *)stage_chunk(cx.stage + h * 4096, cx.lane, 4 * q2 + e);
-                    const int j = 16 * h + 8 * q2;
-#pragma unroll
-                    for (int hh = 0; hh < 2; hh++) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int e = 0; e < 8; e += 2) {
-                            const float4 b4 = __ldg(bq + (hh * 64 + 2 * (j + e)) / 4);  // bias of pairs j+e, j+e+1
-                            float2 f[2];
-#pragma unroll
-                            for (int u = 0; u < 2; u++) {
-                                const float cosv = u ? a[e >> 1].z : a[e >> 1].x, sinv = u ? a[e >> 1].w : a[e >> 1].y;
-                                const int n = hh * 64 + 2 * (j + e + u);
-                                const float2 fb = mul2(add2(make_float2(acc[n], acc[n + 1]),
-                                                            u ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y)), sc2);
-                                // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin)
-                                f[u] = fma2(make_float2(fb.y, fb.x), make_float2(-sinv, sinv), mul2(fb, make_float2(cosv, cosv)));
-                            }
-                            w[e >> 1] = e4m3x2(f[0].x, f[0].y) | (e4m3x2(f[1].x, f[1].y) << 16);
-                        }
-                        o[hh][2 * h + q2] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
+                for (int u = 0; u < 2; u++) {
+                    const float cosv = u ? a.z : a.x, sinv = u ? a.w : a.y;
+                    const float2 fb = mul2(fma2(make_float2(v[4 * e + 2 * u], v[4 * e + 2 * u + 1]), s2,
+                                                u ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y)), sc2);
+                    // (f0, f1) -> (f0 cos - f1 sin, f1 cos + f0 sin)
+                    f[u] = fma2(make_float2(fb.y, fb.x), make_float2(-sinv, sinv), mul2(fb, make_float2(cosv, cosv)));
                 }
+                w[e] = e4m3x2(f[0].x, f[0].y) | (e4m3x2(f[1].x, f[1].y) << 16);
             }
         }
-        __syncwarp();
-#pragma unroll
-        for (int hh = 0; hh < 2; hh++)
-#pragma unroll
-            for (int q = 0; q < 4; q++) *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + q) = o[hh][q];
-        __syncwarp();
-        uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int pc = i * 32 + cx.lane;          // piece: head hh, row r, 16-byte chunk ch
-            const int hh = pc >> 7, r = (pc >> 2) & 31, ch = pc & 3;
-            const int rw = cx.row0 + r;
-            if (rw < p.M) {
-                const int s = rw / p.L, tt = rw - s * p.L;
-                *(uint4 *)(dst + ((((size_t)s * NH + head0 + hh) * p.L + tt) << 6) + ch * 16) =
-                    *(const uint4 *)stage_chunk(cx.stage, r, 4 * hh + ch);
-            }
+        const int rw = cx.row0 + cx.lane;
+        if (rw < p.M) {
+            uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
+            const int sq = rw / p.L, tt = rw - sq * p.L;
+            const int head = ((cx.col0 & 1023) >> 6) + hh;
+            uint4 *o = (uint4 *)(dst + ((((size_t)sq * NH + head) * p.L + tt) << 6) + 32 * h);
+            o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            o[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
-        __syncwarp();
+    }
+    __device__ __forceinline__ static void finish(const Params &, const EpiCtx &, State &) { __syncwarp(); }
+    // the non-streaming call (a block-scaled weight): acc arrives dequantised, 128 columns
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &st)
+    {
+#pragma unroll
+        for (int c = 0; c < 4; c++) apply_chunk(p, acc + 32 * c, 1.0f, c, cx, st);
     }
 };
 
@@ -216,40 +195,60 @@ __device__ __forceinline__ float2 gelu_erf2(float2 v)
 }
 
 // ---- fc1 + GELU: u8 = E4M3(rs * gelu(acc + b1)), gelu(v) = v (1 + erf(v / sqrt 2)) / 2 ----
-// The warp's 32 rows x 128 units leave through one TMA store (128-byte rows, 128B swizzle: the staging layout).
+// A streaming epilogue: each 32-column chunk of the accumulator is turned into 32 E4M3 bytes of the warp's staging
+// rows as soon as its TMEM load lands; the warp's 32 rows x 128 units then leave through one TMA store (128-byte
+// rows, 128B swizzle: the staging layout).
 struct EpiPxFC1 {
     struct Params {
         const float *b1, *rs;
         int M;
     };
     using State = NoState;
+    static constexpr bool STREAM = true;
     __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
-    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
-    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
+    __device__ __forceinline__ static void begin(const Params &, const EpiCtx &cx, State &)
+    {
+        if (cx.lane == 0) bulk_wait_read0();  // the previous tile's store has read the staging rows
+        __syncwarp();
+    }
+    __device__ __forceinline__ static void apply_chunk(const Params &p, const float *v, float s, int c,
+                                                       const EpiCtx &cx, State &)
     {
         if (cx.col0 >= PX_HID) return;  // warp-uniform: the half of the last tile past the units
-        if (cx.lane == 0) bulk_wait_read0();
-        __syncwarp();
-        const float4 *b4p = (const float4 *)(p.b1 + cx.col0), *r4p = (const float4 *)(p.rs + cx.col0);
+        const float4 *b4p = (const float4 *)(p.b1 + cx.col0 + 32 * c), *r4p = (const float4 *)(p.rs + cx.col0 + 32 * c);
+        const float2 s2 = make_float2(s, s);
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
+        for (int h = 0; h < 2; h++) {
             uint32_t w[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const float4 b4 = __ldg(b4p + 4 * c + e), r4 = __ldg(r4p + 4 * c + e);
-                const float *a = acc + 16 * c + 4 * e;
-                const float2 g0 = mul2(gelu_erf2(add2(make_float2(a[0], a[1]), make_float2(b4.x, b4.y))), make_float2(r4.x, r4.y));
-                const float2 g1 = mul2(gelu_erf2(add2(make_float2(a[2], a[3]), make_float2(b4.z, b4.w))), make_float2(r4.z, r4.w));
+                const float4 b4 = __ldg(b4p + 4 * h + e), r4 = __ldg(r4p + 4 * h + e);
+                const float *a = v + 16 * h + 4 * e;
+                const float2 g0 = mul2(gelu_erf2(fma2(make_float2(a[0], a[1]), s2, make_float2(b4.x, b4.y))),
+                                       make_float2(r4.x, r4.y));
+                const float2 g1 = mul2(gelu_erf2(fma2(make_float2(a[2], a[3]), s2, make_float2(b4.z, b4.w))),
+                                       make_float2(r4.z, r4.w));
                 w[e] = e4m3x2(g0.x, g0.y) | (e4m3x2(g1.x, g1.y) << 16);
             }
-            *(uint4 *)stage_chunk(cx.stage, cx.lane, c) = make_uint4(w[0], w[1], w[2], w[3]);
+            *(uint4 *)stage_chunk(cx.stage, cx.lane, 2 * c + h) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+    }
+    __device__ __forceinline__ static void finish(const Params &p, const EpiCtx &cx, State &)
+    {
+        if (cx.col0 >= PX_HID) return;
         fence_proxy_async_smem();
         __syncwarp();
         if (cx.lane == 0 && cx.row0 < p.M) {
             tma_store_2d(cx.tmC, cx.stage, cx.col0, cx.row0);
             bulk_commit();
         }
+    }
+    // the non-streaming call (a block-scaled weight): acc arrives dequantised, 128 columns
+    __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &st)
+    {
+#pragma unroll
+        for (int c = 0; c < 4; c++) apply_chunk(p, acc + 32 * c, 1.0f, c, cx, st);
+        finish(p, cx, st);
     }
 };
 
