@@ -244,6 +244,7 @@ def run_ours(args, rank, world, local):
     # ---- roofline of the dominant kernel (fc1) from one direct forward with per-kernel events ----
     prof = eng.profile()
     sparse_kinds = eng.sparse_kinds()
+    block_scale_kinds = eng.block_scale_kinds()
     fc1_sparse = bool(sparse_kinds & 4)
     fc1_ms = prof["fc1"] / 24
     rows = nb * 1025
@@ -269,9 +270,10 @@ def run_ours(args, rank, world, local):
                                         "preprocessed on the device" if args.mix else ""),
                            "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
                            "weights": ("random-init, E4M3 with one fp32 scale per tensor (eva02.bin v3), fp16 head"
-                                       if args.v3 else "random-init, E4M3 with fp32 scales per 128x128 block") +
+                                       if args.v3 else "random-init, E4M3 with fp32 scales per 128x128 block" +
+                                       (" (powers of two)" if args.pow2 else "")) +
                                       (", QKV / O / W12 / W2 2:4-pruned by magnitude" if args.sparse else ""),
-                           "sparse_kinds": sparse_kinds,
+                           "sparse_kinds": sparse_kinds, "block_scale_kinds": block_scale_kinds,
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
                 "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": args.batch * 1024 * 592 * 2,
                         "d2h_bytes_per_step": args.batch * args.nt * 4},
@@ -322,6 +324,8 @@ def main():
     ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
     ap.add_argument("--sparse", action="store_true", help="config 5: 2:4-pruned projections on the sparse kernels")
     ap.add_argument("--v3", action="store_true", help="weights in the reference's v3 format (per-tensor scales)")
+    ap.add_argument("--pow2", action="store_true",
+                    help="block scales rounded up to powers of two: fc1 on the tensor core's own block scaling")
     ap.add_argument("--mix", action="store_true",
                     help="inputs: whole images + quadrant crops of 896^2 sources, preprocessed on the device (the "
                          "default for config 4: --nt 13461 --batch 32)")
@@ -333,6 +337,8 @@ def main():
     args.mix = args.mix or (args.nt == 13461 and args.batch == 32)
     if args.v3:
         MODEL_KW.update(version=3, head_fp8=False)
+    if args.pow2:
+        MODEL_KW["pow2"] = True
     if args.sparse:
         MODEL_KW["prune24"] = True
         os.environ.setdefault("XTB_SPARSE", "1")  # the engine's sparse kernels are opt-in

@@ -103,6 +103,10 @@ int eva_launches_per_forward(eva *e);
  * the environment at open, the kinds whose weights are 2:4 along k in every layer (as prune24.py writes them);
  * otherwise 0 (the dense kernels are faster on the same weights). */
 int eva_sparse_kinds(eva *e);
+/* Projection kinds (bit 0 QKV, 1 O, 2 W12, 3 W2) running on the tensor core's own block scaling: block-scaled (v4)
+ * weights whose block scales are all powers of two (W12; XTB_MX=0 in the environment at open keeps the promoting
+ * kernel). */
+int eva_block_scale_kinds(eva *e);
 /* One direct (non-graph) forward on device 0 with an event after every kernel; per-kernel-kind milliseconds into
  * ms[kinds] (names from eva_prof_name), returns the number of kinds or -1. Mirrors the reference's EVA_PROF
  * probe (eva.h:312-339). */
@@ -180,6 +184,16 @@ int xtb_sparse24_compress(const uint8_t *w, int n, int k, uint8_t *vals, uint8_t
 /* out[m][n] (fp32) = ascale * sum_k x[m][k] W[n][k] * wscale[n / 128][k / 128], W compressed (device pointers). */
 int xtb_gemm_sp_e4m3_f32(const uint8_t *x, int m, int k, const uint8_t *vals, const uint8_t *meta, int n,
                          const float *wscale, float ascale, float *out, void *stream);
+/* Block scales that are all powers of two run on the tensor core's own block scaling (tcgen05.mma
+ * kind::mxf8f6f4.block_scale) instead of promoting every 128-deep K block through the epilogue. xtb_sf_image (host
+ * memory in and out) turns block scales ws [ceil(n/128)][ceil(k/128)] into the scale-factor image that kernel reads
+ * (xtb_sf_image_bytes(n, k) bytes); it returns -1 if some scale is not a power of two. xtb_fc1_mx is xtb_fc1 with
+ * the weight's scale-factor image sf (device memory) in place of ws: the same results up to the fp32 summation
+ * order. */
+size_t xtb_sf_image_bytes(int n, int k);
+int xtb_sf_image(const float *ws, int n, int k, uint8_t *img);
+int xtb_fc1_mx(const uint8_t *h, int rows, const uint8_t *w, const uint8_t *sf, float ascale, uint8_t *h8, float *stat,
+               const float *rs, void *stream);
 /* As xtb_qkv / xtb_oproj / xtb_fc1 / xtb_fc2 with the weight compressed (vals, meta) and its block scales ws. */
 int xtb_qkv_sp(const uint8_t *h, int rows, const uint8_t *vals, const uint8_t *meta, const float *ws, float ascale,
                uint8_t *q8, uint8_t *k8, uint8_t *v8, const float *cs, float cq, float ck, float cv, void *stream);

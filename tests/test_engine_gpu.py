@@ -39,11 +39,15 @@ def models(tmp_path_factory):
         # the reference's format pruned as prune24.py does: the sparse kernels without block-scale promotion
         "v3_l24_p": M.write_synthetic(os.path.join(d, "g.bin"), seed=10, nl=24, version=3, head_fp8=False,
                                       prune24=True),
+        # power-of-two block scales: fc1 on the tensor core's own block scaling
+        "v4_l2_pow2": M.write_synthetic(os.path.join(d, "h.bin"), seed=11, nl=2, ln_noise=1.0, head_fp8=True, pow2=True),
+        "v4_l24_pow2": M.write_synthetic(os.path.join(d, "i.bin"), seed=12, nl=24, head_fp8=True, pow2=True),
     }
 
 
 @pytest.mark.parametrize("name,nimg", [("v4_l2_h8", 3), ("v4_l2_h16", 2), ("v4_l24_h8", 1), ("v3_l24", 1),
-                                       ("v4_l2_p", 3), ("v4_l24_p", 1), ("v3_l24_p", 1)])
+                                       ("v4_l2_p", 3), ("v4_l24_p", 1), ("v3_l24_p", 1), ("v4_l2_pow2", 3),
+                                       ("v4_l24_pow2", 1)])
 def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
     from oracle import oracle as O
     from xtagger_b200 import model as M
@@ -60,6 +64,7 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
         try:
             got = eng.run(x)
             assert eng.sparse_kinds() == (15 if name.endswith("_p") else 0)
+            assert eng.block_scale_kinds() == (4 if name.endswith("_pow2") else 0)
         finally:
             eng.close()
     finally:

@@ -209,3 +209,49 @@ def test_pool_ln_head(xlib, cuda, O, head8):
     np.testing.assert_allclose(G.host(dpool), pool, rtol=1e-4, atol=1e-4)
     G.assert_f16_close(G.host(dpn).view(np.uint16), pn, 1e-2, "pn")
     np.testing.assert_allclose(G.host(out), want, atol=2e-3)
+
+
+def test_fc1_mx_block_scale(xlib, cuda, O):
+    """Power-of-two block scales on the tensor core's own block scaling (kind::mxf8f6f4.block_scale): the same h8
+    as the oracle (and as the promoting kernel on the same weights), codes equal or one step apart."""
+    import ctypes as C
+    import torch
+    from xtagger_b200 import model as M
+    rng = np.random.default_rng(17)
+    h = _act8(rng, ROWS, D, O)
+    w12 = np.zeros((N12, D), np.float32)
+    w12[:2730] = rng.standard_normal((2730, D), dtype=np.float32) * 0.02
+    w12[HIDP:HIDP + 2730] = rng.standard_normal((2730, D), dtype=np.float32) * 0.02
+    w12[:, :128] *= 8.0                              # block scales that differ across K blocks and N blocks
+    w12[1000:1200] *= 0.25
+    w, ws = M.quant_blocks(M.interleave_gx(w12), pow2=True)
+    assert len(np.unique(ws)) > 2
+    adq = 10 / 448
+    rs = np.full(HIDP, 448 / 3.0, np.float32)
+    acc = O.gemm_e4m3(h, w, ws, adq)
+    want = np.empty((ROWS, HIDP), np.uint8)
+    s, q = np.empty(ROWS), np.empty(ROWS)
+    O.lib().or_fc1_epilogue(acc, ROWS, rs, want, s, q)
+    img = np.zeros(xlib.xtb_sf_image_bytes(N12, D), np.uint8)
+    assert xlib.xtb_sf_image(ws.ctypes.data_as(C.c_void_p), N12, D, img.ctypes.data_as(C.c_void_p)) == 0
+    bad = ws.copy()
+    bad[0, 0] *= 1.5
+    assert xlib.xtb_sf_image(bad.ctypes.data_as(C.c_void_p), N12, D, img.copy().ctypes.data_as(C.c_void_p)) == -1
+    outs = []
+    for mx in (False, True):
+        h8 = G.zeros((ROWS, HIDP), torch.uint8)
+        stat = G.zeros((43, ROWS, 2), torch.float32)
+        if mx:
+            rc = xlib.xtb_fc1_mx(G.P(G.dev(h)), ROWS, G.P(G.dev(w)), G.P(G.dev(img)), adq, G.P(h8), G.P(stat),
+                                 G.P(G.dev(rs)), None)
+        else:
+            rc = xlib.xtb_fc1(G.P(G.dev(h)), ROWS, G.P(G.dev(w)), G.P(G.dev(ws)), adq, G.P(h8), G.P(stat),
+                              G.P(G.dev(rs)), None)
+        assert rc == 0
+        G.check_error_word(xlib)
+        got = G.host(h8)
+        G.assert_e4m3_close(got, want, 1, 0.99, f"h8 (mx {mx})")
+        st = G.host(stat).astype(np.float64).sum(0)
+        np.testing.assert_allclose(st[:, 1], q, rtol=1e-3)
+        outs.append(got)
+    G.assert_e4m3_close(outs[1], outs[0], 1, 0.99, "mx vs promote")

@@ -111,6 +111,30 @@ int xtb_fc1(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float
     return launch_fc1(A, W, ascale, rows, h8, (float2 *)stat, rs, S(stream));
 }
 
+size_t xtb_sf_image_bytes(int n, int k) { return n > 0 && k > 0 ? sf_image_bytes(n, k) : 0; }
+
+int xtb_sf_image(const float *ws, int n, int k, uint8_t *img)
+{
+    if (!ws || !img || n <= 0 || k <= 0) return -1;
+    return sf_image(ws, n, k, img);
+}
+
+int xtb_fc1_mx(const uint8_t *h, int rows, const uint8_t *w, const uint8_t *sf, float ascale, uint8_t *h8, float *stat,
+               const float *rs, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (!rows_ok(rows, "xtb_fc1_mx") || !sf || make_operand(&A, h, rows, D, 128) ||
+        make_operand(&W.op, w, N12, D, 256))
+        return -1;
+    W.ws = nullptr;
+    W.n = N12;
+    W.k = D;
+    W.sf = sf;
+    W.sf_nbp = (((N12 + 127) / 128) + 1) & ~1;
+    return launch_fc1(A, W, ascale, rows, h8, (float2 *)stat, rs, S(stream));
+}
+
 int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, float *stat,
             const float *c, const float *d, void *stream)
 {

@@ -65,6 +65,7 @@ struct Replica {
     Operand op_in, op_pe, op_h, op_h8, op_hw, op_pn;
     Operand op_h_sp, op_h8_sp;     // the same activations in the sparse kernels' token boxes
     uint8_t *spw = nullptr;        // compressed 2:4 weights (Impl::sp_host on this device)
+    uint8_t *sfimg = nullptr;      // fc1 scale-factor images (power-of-two block scales), every layer
     Weight8 whead;
     Attn attn;
     cudaGraphExec_t graph = nullptr;   // the forward reading input buffer 0 (in)
@@ -377,6 +378,27 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     if (off < 0) return -1;
     RCK(head_layout(im, r, e, (size_t)off));
     if (!im->sp_ready) RCK(sparse_prepare(im, r, hostblob));
+    if (im->ver == 4 && !im->sp_mask) {
+        // fc1 weights whose block scales are all powers of two run on the tensor core's own block scaling (no
+        // per-K-block promotion); XTB_MX=0 in the environment keeps the promoting kernel
+        const char *env = getenv("XTB_MX");
+        const size_t per = sf_image_bytes(N12, D);
+        std::vector<uint8_t> img(per * im->nl);
+        bool all = !(env && env[0] == '0');
+        for (int i = 0; i < im->nl && all; i++) {
+            const float *ws_h = (const float *)(hostblob + ((const uint8_t *)r.L[i].w[2].ws - r.wts));
+            all = sf_image(ws_h, N12, D, img.data() + (size_t)i * per) == 0;
+        }
+        if (all) {
+            ECK(cudaMalloc(&r.sfimg, img.size()));
+            ECK(cudaMemcpyAsync(r.sfimg, img.data(), img.size(), cudaMemcpyHostToDevice, r.st));
+            ECK(cudaStreamSynchronize(r.st));  // the host image is pageable
+            for (int i = 0; i < im->nl; i++) {
+                r.L[i].w[2].sf = r.sfimg + (size_t)i * per;
+                r.L[i].w[2].sf_nbp = ((N12 + 127) / 128 + 1) & ~1;
+            }
+        }
+    }
     if (im->sp_mask) {
         ECK(cudaMalloc(&r.spw, im->sp_host.size()));
         ECK(cudaMemcpyAsync(r.spw, im->sp_host.data(), im->sp_host.size(), cudaMemcpyHostToDevice, r.st));
@@ -838,7 +860,8 @@ void eva_close(eva *e)
             if (r.in_ready[k]) cudaEventDestroy(r.in_ready[k]);
             if (r.in_free[k]) cudaEventDestroy(r.in_free[k]);
         }
-        void *bufs[] = {r.in, r.in_b, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp, r.spw};
+        void *bufs[] = {r.in, r.in_b, r.x, r.h, r.q8, r.k8, r.v8, r.h8, r.stat, r.pool, r.pn, r.pn8, r.out, r.wts, r.sexp, r.spw,
+                        r.sfimg};
         for (void *p : bufs)
             if (p) cudaFree(p);
         if (r.errh) cudaFreeHost(r.errh);
@@ -925,6 +948,16 @@ void *eva_output(eva *e, int i)
     Impl *im = I(e);
     if (!im || eva_ready(e) || i < 0 || (size_t)i >= im->reps.size()) return nullptr;
     return (void *)im->reps[i].out;
+}
+
+int eva_block_scale_kinds(eva *e)
+{
+    Impl *im = I(e);
+    if (!im || eva_ready(e) || im->reps[0].L.empty()) return 0;
+    int m = 0;
+    for (int g = 0; g < NG; g++)
+        if (im->reps[0].L[0].w[g].sf) m |= 1 << g;
+    return m;
 }
 
 int eva_sparse_kinds(eva *e)

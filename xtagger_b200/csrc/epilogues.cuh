@@ -180,6 +180,7 @@ struct EpiFC1 {
         int M;
     };
     using State = NoState;
+    static constexpr int STAGING_PER_WARP = 2048;  // 32 rows x 64 units of E4M3
     __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)

@@ -5,6 +5,7 @@
 #include "attention.cuh"
 #include "epilogues.cuh"
 #include "gemm.cuh"
+#include "gemm_mx.cuh"
 #include "gemm_sp.cuh"
 #include "host.h"
 #include "ops.h"
@@ -116,6 +117,62 @@ static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const flo
 }
 
 static int kb(int k) { return (k + 127) / 128; }
+
+size_t sf_image_bytes(int n, int k) { return (size_t)kb(k) * ((kb(n) + 1) & ~1) * 512; }
+
+int sf_image(const float *ws, int n, int k, uint8_t *img)
+{
+    const int nbn = kb(n), nbk = kb(k), nbp = (nbn + 1) & ~1;
+    for (int i = 0; i < nbn * nbk; i++) {
+        uint32_t u;
+        memcpy(&u, ws + i, 4);
+        const uint32_t e = (u >> 23) & 0xFF;
+        if ((u & 0x807FFFFFu) || e == 0 || e == 0xFF) return -1;  // positive normal powers of two only
+    }
+    for (int q = 0; q < nbk; q++)
+        for (int b = 0; b < nbp; b++) {
+            uint8_t e = 127;  // padding N block: 2^0
+            if (b < nbn) {
+                uint32_t u;
+                memcpy(&u, ws + (size_t)b * nbk + q, 4);
+                e = (uint8_t)((u >> 23) & 0xFF);
+            }
+            memset(img + ((size_t)q * nbp + b) * 512, e, 512);
+        }
+    return 0;
+}
+
+// One launch of the block-scaled GEMM on the tensor core's own scaling (power-of-two block scales, w.sf).
+template <class Epi>
+static int run_gemm_mx(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep,
+                       cudaStream_t st, const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
+{
+    using Cfg = GemmMxCfg<StagingOf<Epi>::v>;
+    auto kern = k_gemm_mx<Epi>;
+    if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
+    if (!w.sf || a.row_bytes != w.op.row_bytes || M <= 0 || a.box_rows != A_BOX_ROWS || w.op.box_rows != Cfg::BN) {
+        fprintf(stderr, "eva: mx gemm operands (scale image %p, K bytes %d vs %d, boxes %d / %d rows, M %d)\n",
+                (const void *)w.sf, a.row_bytes, w.op.row_bytes, a.box_rows, w.op.box_rows, M);
+        return -1;
+    }
+    const int dev = current_device();
+    GemmArgs g{};
+    g.M = M;
+    g.N = w.n;
+    g.kiters = (a.row_bytes + 127) / 128;
+    g.m_tiles = (M + 127) / 128;
+    g.n_tiles = (w.n + Cfg::BN - 1) / Cfg::BN;
+    g.ascale = ascale;
+    g.wsu = 1.0f;
+    g.err = err ? err : error_word(dev);
+    GemmMxArgs mx{w.sf, w.sf_nbp};
+    const int total = g.m_tiles * g.n_tiles;
+    int grid = num_sms(dev);
+    if (grid > total) grid = total;
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, w.op.map, tmc ? *tmc : a.map, g, mx, ep);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
 
 // Kernel of each projection (true: CTA pair), from timing both inside the batch-64 forward: the pair wins where the
 // operand feed bounds the main loop (fc2: K = 2736, A streamed from DRAM, 5.6 against 6.4 ms per forward) and for
@@ -256,6 +313,7 @@ int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8
     CUtensorMap hm;  // h8 [rows][2736] E4M3, stored in boxes of 64 units x 32 rows (64B swizzle)
     if (make_tmap_2d(&hm, h8, HIDP, (uint64_t)rows, HIDP, 64, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     EpiFC1::Params p{stat, rs, rows};
+    if (w.sf) return run_gemm_mx<EpiFC1>(h, w, rows, ascale, p, st, &hm);  // power-of-two block scales
     return run_proj<EpiFC1, W_FC1>(h, w, rows, ascale, p, st, &hm);
 }
 
@@ -454,6 +512,7 @@ int prepare_kernels()
         if (set_smem(k, SpCfg::SMEM)) return -1;
     if (set_smem((const void *)k_ln_e4m3, LN_SMEM)) return -1;
     if (set_smem((const void *)k_attention<AttEva>, ATT_SMEM)) return -1;
+    if (set_smem((const void *)k_gemm_mx<EpiFC1>, GemmMxCfg<StagingOf<EpiFC1>::v>::SMEM)) return -1;
     return 0;
 }
 

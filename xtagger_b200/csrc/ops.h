@@ -39,7 +39,15 @@ struct Weight8 {
     const float *ws;
     int n, k;
     float uniform = 0.0f;
+    // every block scale a power of two: its scale-factor image ([k/128][sf_nbp][512] bytes, each record one UE8M0
+    // exponent repeated) for the tensor core's own block scaling (gemm_mx.cuh); null otherwise
+    const uint8_t *sf = nullptr;
+    int sf_nbp = 0;
 };
+// Scale-factor image of block scales ws [ceil(n/128)][ceil(k/128)] (host memory) into img (sf_image_bytes(n, k)
+// bytes): 0 if every scale is a power of two (a normal float with a zero mantissa), else -1 and img untouched.
+size_t sf_image_bytes(int n, int k);
+int sf_image(const float *ws, int n, int k, uint8_t *img);
 
 struct Attn {
     CUtensorMap tq, tk, tv;

@@ -287,6 +287,25 @@ __device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc_
     asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc_) : "memory");
 }
 
+// 32 lanes x 128 bits from shared memory (32 rows of 16 bytes) into the same 32-lane slice of all four lane groups
+// (warpx4): four TMEM columns at taddr across the 128 lanes. The copy into a block-scaled MMA's scale factors.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc_)
+{
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc_) : "memory");
+}
+
+// D[tmem] (+)= (A[smem] x 2^sfa) (B[smem] x 2^sfb)^T, kind::mxf8f6f4 block-scaled (E4M3 operands, one UE8M0 scale
+// per 32 K elements and row, read from tensor memory at sfa / sfb).
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                        uint32_t sfb, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // The same wait with the 32 registers of an earlier tcgen05.ld tied to it, so that no use of them is scheduled before
 // it (the loads write their destinations asynchronously).
@@ -428,6 +447,12 @@ __device__ __forceinline__ uint64_t sdesc_rows16(uint32_t saddr)
 __host__ __device__ constexpr uint32_t idesc_m128(uint32_t n)
 {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+}
+// Block-scaled kind::mxf8f6f4, M = 128 (E4M3 A and B, K-major, UE8M0 scales: bit 23): B's scale-factor byte id in
+// bits 4-5, A's in bits 29-30 (which of the four 32-K scale bytes of a TMEM word an instruction reads).
+__host__ __device__ constexpr uint32_t idesc_mx_m128(uint32_t n, uint32_t sfa_id, uint32_t sfb_id)
+{
+    return ((sfb_id & 3u) << 4) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) | ((sfa_id & 3u) << 29);
 }
 // The same with A 2:4-sparse (bit 2; K = 64 logical elements per instruction).
 __host__ __device__ constexpr uint32_t idesc_sp_m128(uint32_t n) { return idesc_m128(n) | (1u << 2); }

@@ -106,6 +106,9 @@ class Engine:
         """Device address of the i-th device's resident scores (what forward_resident writes)."""
         return self.lib.eva_output(C.byref(self.e), i)
 
+    def block_scale_kinds(self):
+        return self.lib.eva_block_scale_kinds(C.byref(self.e))
+
     def launches_per_forward(self):
         return self.lib.eva_launches_per_forward(C.byref(self.e))
 

@@ -81,6 +81,7 @@ _SIGS = {
     "eva_output": (_P, [C.POINTER(Eva), C.c_int]),
     "eva_launches_per_forward": (C.c_int, [C.POINTER(Eva)]),
     "eva_sparse_kinds": (C.c_int, [C.POINTER(Eva)]),
+    "eva_block_scale_kinds": (C.c_int, [C.POINTER(Eva)]),
     "eva_profile": (C.c_int, [C.POINTER(Eva), _P, C.c_int]),
     "eva_prof_name": (C.c_char_p, [C.c_int]),
     "xtb_gemm_e4m3_f32": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_float, _P, _P]),
@@ -89,6 +90,9 @@ _SIGS = {
     "xtb_attention": (C.c_int, [_P, _P, _P, C.c_int, _P, C.c_float, C.c_float, _P]),
     "xtb_oproj": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P]),
     "xtb_fc1": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P]),
+    "xtb_sf_image_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "xtb_sf_image": (C.c_int, [_P, C.c_int, C.c_int, _P]),
+    "xtb_fc1_mx": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P]),
     "xtb_fc2": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
     "xtb_patch_embed": (C.c_int, [_P, C.c_int, _P, _P, _P, _P]),
     "xtb_pool_ln": (C.c_int, [_P, C.c_int, _P, _P, _P, _P, _P, C.c_float, _P]),

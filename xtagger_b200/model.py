@@ -40,8 +40,10 @@ def e4m3_decode(b):
     return np.asarray(b, np.uint8).view(ml_dtypes.float8_e4m3fn).astype(np.float32)
 
 
-def quant_blocks(w, blk=128):
-    """E4M3 with one fp32 scale per blk x blk block: scale = max|block| / 448 (1 for an all-zero block)."""
+def quant_blocks(w, blk=128, pow2=False):
+    """E4M3 with one fp32 scale per blk x blk block: scale = max|block| / 448 (1 for an all-zero block); with pow2 the
+    scale is rounded up to a power of two (the block's largest value then lands in [224, 448]), which the tensor
+    core applies itself as an UE8M0 scale factor."""
     n, k = w.shape
     nb, kb = -(-n // blk), -(-k // blk)
     wp = np.zeros((nb * blk, kb * blk), np.float32)
@@ -49,6 +51,8 @@ def quant_blocks(w, blk=128):
     v = wp.reshape(nb, blk, kb, blk)
     s = np.abs(v).max(axis=(1, 3)).astype(np.float32) / E4M3_MAX
     s[s == 0] = 1.0
+    if pow2:
+        s = np.exp2(np.ceil(np.log2(s.astype(np.float64)))).astype(np.float32)
     q = _e4m3(v / s[:, None, :, None]).reshape(nb * blk, kb * blk)[:n, :k]
     return np.ascontiguousarray(q), s
 
@@ -128,14 +132,15 @@ class _Blob:
         self.n += len(b)
 
 
-def write_synthetic(path, seed=0, nt=10861, nl=24, version=4, head_fp8=True, ln_noise=0.0, std=0.02, prune24=False):
+def write_synthetic(path, seed=0, nt=10861, nl=24, version=4, head_fp8=True, ln_noise=0.0, std=0.02, prune24=False,
+                    pow2=False):
     """Random-init EVA02-L tagger in eva02.bin format.
 
     Linears N(0, std) quantised to E4M3 (v4: per 128 x 128 block; v3: per tensor); LayerNorm gamma = 1 and
     beta = 0, perturbed by N(0, 0.1 ln_noise) when ln_noise > 0 (so that every folded term is exercised);
     pos, cls, patch embedding N(0, std); EVA02 RoPE table; head bias 0. prune24: the four projections of every
     layer (QKV, O, W12, W2) made 2:4 sparse along k after quantisation (prune24_codes); the folded MLP term c is
-    computed from the pruned W2.
+    computed from the pruned W2. pow2 (v4): the four projections' block scales are powers of two (quant_blocks).
     Static activation scales: closed-form statistics of the random-init network, since LayerNorm outputs have
     unit variance per row: LN outputs amax 8; q / k / v amax 6 ||W row||_2 (max over rows); attention output
     bounded by v's; SwiGLU output 16 sigma_x sigma_g; every one times the reference's 1.25 headroom.
@@ -196,7 +201,7 @@ def write_synthetic(path, seed=0, nt=10861, nl=24, version=4, head_fp8=True, ln_
         mats = []
         for g, w in enumerate((wqkv, wo, w12, wt2)):
             if version == 4:
-                q, s = quant_blocks(w)
+                q, s = quant_blocks(w, pow2=pow2)
                 if prune24:
                     q = prune24_codes(q)
                 table[i, g] = 1.0
