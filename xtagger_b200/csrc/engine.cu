@@ -379,23 +379,41 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     RCK(head_layout(im, r, e, (size_t)off));
     if (!im->sp_ready) RCK(sparse_prepare(im, r, hostblob));
     if (im->ver == 4 && !im->sp_mask) {
-        // fc1 weights whose block scales are all powers of two run on the tensor core's own block scaling (no
-        // per-K-block promotion); XTB_MX=0 in the environment keeps the promoting kernel
+        // projection kinds whose block scales are all powers of two, in every layer, run on the tensor core's own
+        // block scaling (no per-K-block promotion); XTB_MX=0 in the environment keeps the promoting kernels
         const char *env = getenv("XTB_MX");
-        const size_t per = sf_image_bytes(N12, D);
-        std::vector<uint8_t> img(per * im->nl);
-        bool all = !(env && env[0] == '0');
-        for (int i = 0; i < im->nl && all; i++) {
-            const float *ws_h = (const float *)(hostblob + ((const uint8_t *)r.L[i].w[2].ws - r.wts));
-            all = sf_image(ws_h, N12, D, img.data() + (size_t)i * per) == 0;
-        }
-        if (all) {
-            ECK(cudaMalloc(&r.sfimg, img.size()));
-            ECK(cudaMemcpyAsync(r.sfimg, img.data(), img.size(), cudaMemcpyHostToDevice, r.st));
-            ECK(cudaStreamSynchronize(r.st));  // the host image is pageable
-            for (int i = 0; i < im->nl; i++) {
-                r.L[i].w[2].sf = r.sfimg + (size_t)i * per;
-                r.L[i].w[2].sf_nbp = ((N12 + 127) / 128 + 1) & ~1;
+        if (!(env && env[0] == '0')) {
+            size_t per[NG], off[NG], total = 0;
+            int mask = 0;
+            std::vector<uint8_t> img;
+            for (int g = 0; g < NG; g++) {
+                const int n = r.L[0].w[g].n, k = r.L[0].w[g].k;
+                per[g] = sf_image_bytes(n, k);
+                off[g] = total;
+                std::vector<uint8_t> part(per[g] * im->nl);
+                bool all = true;
+                for (int i = 0; i < im->nl && all; i++) {
+                    const float *ws_h = (const float *)(hostblob + ((const uint8_t *)r.L[i].w[g].ws - r.wts));
+                    all = sf_image(ws_h, n, k, part.data() + (size_t)i * per[g]) == 0;
+                }
+                if (!all) continue;
+                mask |= 1 << g;
+                img.insert(img.end(), part.begin(), part.end());
+                total += part.size();
+            }
+            if (mask) {
+                ECK(cudaMalloc(&r.sfimg, img.size()));
+                ECK(cudaMemcpyAsync(r.sfimg, img.data(), img.size(), cudaMemcpyHostToDevice, r.st));
+                ECK(cudaStreamSynchronize(r.st));  // the host image is pageable
+                for (int g = 0; g < NG; g++) {
+                    if (!(mask & (1 << g))) continue;
+                    for (int i = 0; i < im->nl; i++) {
+                        Weight8 &w = r.L[i].w[g];
+                        w.sf = r.sfimg + off[g] + (size_t)i * per[g];
+                        w.sf_nbp = ((w.n + 127) / 128 + 1) & ~1;
+                        RCK(make_operand(&w.op, w.op.ptr, w.n, w.k, 256));  // the block-scaled kernel's 256-row boxes
+                    }
+                }
             }
         }
     }

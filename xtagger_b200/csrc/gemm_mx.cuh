@@ -29,11 +29,13 @@ struct GemmMxCfg {
     static constexpr int EW = 8;
     static constexpr int COLS = BN / (EW / 4);          // 128 accumulator columns per epilogue thread
     static constexpr int STAGING = EW * SPW;
-    static constexpr int STAGES = 4;
+    // as many stages (at most 4) as fit beside the epilogue's staging: 4 with 2 KB per warp, 3 with 4 or 8 KB
+    static constexpr int STAGES_FIT = (232448 - 2048 - STAGING) / (STAGE_BYTES + SF_BYTES);
+    static constexpr int STAGES = STAGES_FIT < 4 ? STAGES_FIT : 4;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * (STAGE_BYTES + SF_BYTES) + STAGING + 512 + 512;
     static constexpr int THREADS = 64 + 32 * EW;
     static constexpr uint32_t SFA_COL = 256, SFB_COL = 288;
-    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(STAGES >= 3 && SMEM <= 232448, "shared memory budget");
 };
 
 // Scale-factor image of a weight: [kiters][nbp][512] bytes, nbp = N blocks rounded up to even.

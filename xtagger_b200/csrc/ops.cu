@@ -196,6 +196,7 @@ template <class Epi, WeightUse U>
 static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep, cudaStream_t st,
                     const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
 {
+    if (w.sf) return run_gemm_mx<Epi>(a, w, M, ascale, ep, st, tmc, err);  // power-of-two block scales
     if (!kPairG[U] && w.uniform > 0.0f) {  // one scale for the whole weight: accumulate over K in TMEM, scale once
         if constexpr (kPair[U])
             return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
@@ -313,7 +314,6 @@ int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8
     CUtensorMap hm;  // h8 [rows][2736] E4M3, stored in boxes of 64 units x 32 rows (64B swizzle)
     if (make_tmap_2d(&hm, h8, HIDP, (uint64_t)rows, HIDP, 64, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return -1;
     EpiFC1::Params p{stat, rs, rows};
-    if (w.sf) return run_gemm_mx<EpiFC1>(h, w, rows, ascale, p, st, &hm);  // power-of-two block scales
     return run_proj<EpiFC1, W_FC1>(h, w, rows, ascale, p, st, &hm);
 }
 
@@ -512,7 +512,11 @@ int prepare_kernels()
         if (set_smem(k, SpCfg::SMEM)) return -1;
     if (set_smem((const void *)k_ln_e4m3, LN_SMEM)) return -1;
     if (set_smem((const void *)k_attention<AttEva>, ATT_SMEM)) return -1;
-    if (set_smem((const void *)k_gemm_mx<EpiFC1>, GemmMxCfg<StagingOf<EpiFC1>::v>::SMEM)) return -1;
+    if (set_smem((const void *)k_gemm_mx<EpiFC1>, GemmMxCfg<StagingOf<EpiFC1>::v>::SMEM) ||
+        set_smem((const void *)k_gemm_mx<EpiQKV>, GemmMxCfg<StagingOf<EpiQKV>::v>::SMEM) ||
+        set_smem((const void *)k_gemm_mx<EpiResid>, GemmMxCfg<StagingOf<EpiResid>::v>::SMEM) ||
+        set_smem((const void *)k_gemm_mx<EpiFC2>, GemmMxCfg<StagingOf<EpiFC2>::v>::SMEM))
+        return -1;
     return 0;
 }
 
