@@ -7,6 +7,9 @@ E4M3 weights (24 layers, 10861 tags, FP8 head).
 --v3 runs the same forward on weights in the reference's own eva02.bin v3 format (one E4M3 scale per tensor, fp16
 head): the GEMMs then accumulate the whole K range in TMEM and scale once, as the reference's kernels do. This is
 the format oracle/ref_time.py times the reference's kernels on.
+Block scales are powers of two by default (max / 448 rounded up, the convention of the tensor core's own block
+scaling): QKV and fc1 then run on tcgen05.mma kind::mxf8f6f4.block_scale with the whole K range in one accumulator;
+--free-scales writes max / 448 scales instead, and every projection promotes its 128-deep K blocks in the epilogue.
 --sparse is config 5: the four projections of every layer 2:4-pruned by magnitude (prune24.py's rule), which the
 engine runs on the sparse tensor cores (tcgen05.mma.sp); global batch 128 unless --batch is given.
 --nt 13461 --batch 32 is config 4 (implies --mix): the inputs are views of seeded 896^2 sources (per source the
@@ -39,7 +42,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "images/sec EVA02-L 448² (1/2/4/8 B200) + FP8 GEMM % of tensor peak"
 NT = 10861
-MODEL_KW = dict(seed=0, nt=NT, nl=24, version=4, head_fp8=True)
+MODEL_KW = dict(seed=0, nt=NT, nl=24, version=4, head_fp8=True, pow2=True)
 FC1_FLOP_PER_ROW = 2.0 * 5472 * 1024
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one fc1 launch in an ncu capture at batch 32
 # (32 x 1025 rows): 39.34 MB + 47.44 MB; the launch at another batch is scaled by the rows it processes.
@@ -271,7 +274,8 @@ def run_ours(args, rank, world, local):
                            "global_batch": args.batch, "per_gpu_batch_rank0": nb, "parallelism": f"dp{world}",
                            "weights": ("random-init, E4M3 with one fp32 scale per tensor (eva02.bin v3), fp16 head"
                                        if args.v3 else "random-init, E4M3 with fp32 scales per 128x128 block" +
-                                       (" (powers of two)" if args.pow2 else "")) +
+                                       (" (max / 448)" if args.free_scales else
+                                        " (powers of two, max / 448 rounded up)")) +
                                       (", QKV / O / W12 / W2 2:4-pruned by magnitude" if args.sparse else ""),
                            "sparse_kinds": sparse_kinds, "block_scale_kinds": block_scale_kinds,
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
@@ -324,8 +328,8 @@ def main():
     ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
     ap.add_argument("--sparse", action="store_true", help="config 5: 2:4-pruned projections on the sparse kernels")
     ap.add_argument("--v3", action="store_true", help="weights in the reference's v3 format (per-tensor scales)")
-    ap.add_argument("--pow2", action="store_true",
-                    help="block scales rounded up to powers of two: fc1 on the tensor core's own block scaling")
+    ap.add_argument("--free-scales", action="store_true",
+                    help="block scales max / 448 instead of powers of two: every projection on the promoting kernels")
     ap.add_argument("--mix", action="store_true",
                     help="inputs: whole images + quadrant crops of 896^2 sources, preprocessed on the device (the "
                          "default for config 4: --nt 13461 --batch 32)")
@@ -337,8 +341,8 @@ def main():
     args.mix = args.mix or (args.nt == 13461 and args.batch == 32)
     if args.v3:
         MODEL_KW.update(version=3, head_fp8=False)
-    if args.pow2:
-        MODEL_KW["pow2"] = True
+    if args.free_scales or args.v3:
+        MODEL_KW["pow2"] = False
     if args.sparse:
         MODEL_KW["prune24"] = True
         os.environ.setdefault("XTB_SPARSE", "1")  # the engine's sparse kernels are opt-in

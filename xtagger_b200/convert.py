@@ -11,7 +11,8 @@ from the upstream ONNX graph, absent here; everything after that is the same):
   * the MLP LayerNorm folded into fc2: W~ = gamma W2, d = W2 beta, c = W~ 1 from the quantised W~ (export_eva.py:98-
     118), rs = 448 / (1.25 amax(h / s));
   * E4M3 with one scale per tensor (v3, export_eva.py:64-66), or with one fp32 scale per 128 x 128 block (v4, this
-    library's block-scaled format); table [24][12] = w_dq x 4, a_dq x 4 (calibrated amax x 1.25 / 448), q, k, v;
+    library's block-scaled format; powers of two by default, which the tensor core applies itself); table [24][12] =
+    w_dq x 4, a_dq x 4 (calibrated amax x 1.25 / 448), q, k, v;
   * every tensor on a 256-byte boundary, header "EVA2", version, tags, bytes, zero padding to 256 (export_eva.py:
     119-153); the head stays fp16.
 
@@ -46,9 +47,10 @@ def fp8_tensor(w):
     return M._e4m3(w / sc), sc
 
 
-def convert(f, calib, path, version=3):
-    """Write eva02.bin (version 3: per-tensor E4M3; 4: 128 x 128 block scales) from the float model f and the
-    calibration statistics (amax [nl][4][2736], qkv [nl][3][1024], h [nl][2736])."""
+def convert(f, calib, path, version=3, pow2=True):
+    """Write eva02.bin (version 3: per-tensor E4M3; 4: 128 x 128 block scales, powers of two unless pow2 is false, so
+    that the engine's block-scaled MMA applies them) from the float model f and the calibration statistics (amax
+    [nl][4][2736], qkv [nl][3][1024], h [nl][2736])."""
     assert version in (3, 4)
     from xtagger_b200 import calib as CB
     amax, qkvmax, hmax = calib
@@ -101,7 +103,7 @@ def convert(f, calib, path, version=3):
                 q, table[b, k] = fp8_tensor(w)
                 mats.append((q, None, M.e4m3_decode(q) * table[b, k]))
             else:
-                q, sc = M.quant_blocks(w)
+                q, sc = M.quant_blocks(w, pow2=pow2)
                 table[b, k] = 1.0
                 mats.append((q, sc, M.dequant_blocks(q, sc)))
             table[b, 4 + k] = float((a[k] / s[k]).max()) * HEADROOM / E4M3
@@ -163,10 +165,11 @@ def main():
     ap.add_argument("out", help="eva02.bin to write")
     ap.add_argument("calib", help="calibration statistics (.calib, as written by xtagger_b200.calib.write_calib)")
     ap.add_argument("--v4", action="store_true", help="128 x 128 block scales instead of one scale per tensor")
+    ap.add_argument("--free-scales", action="store_true", help="v4 block scales max / 448, not powers of two")
     a = ap.parse_args()
     from xtagger_b200 import calib as CB
     f = dict(np.load(a.model))
-    convert(f, CB.read_calib(a.calib, CB.num_layers(f)), a.out, 4 if a.v4 else 3)
+    convert(f, CB.read_calib(a.calib, CB.num_layers(f)), a.out, 4 if a.v4 else 3, pow2=not a.free_scales)
     print(f"{a.out}: v{4 if a.v4 else 3}, {f['head.weight'].shape[0]} tags")
 
 
