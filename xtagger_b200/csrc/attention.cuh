@@ -74,6 +74,30 @@ __device__ __forceinline__ float ex2(float x)
 }
 
 
+// 2^x on the FMA and ALU pipes, for the share of the softmax's exponentials taken off the MUFU unit (the kernel's
+// limiter): Cody-Waite style reduction x = n + f with n = round(x) by the 1.5 x 2^23 shifter (no conversion
+// instruction), f in [-0.5, 0.5]; 2^f by a degree-5 polynomial fitted for this library to 2^f on [-0.5, 0.5]
+// (relative error 2.0e-7 in fp32 Horner form, the order of ex2.approx's own); 2^n added into the exponent field.
+// Arguments below -126 are clamped there (2^-126 rounds to E4M3 zero and adds nothing measurable to a row sum);
+// arguments stay below RESCALE = 8 by the softmax's construction.
+constexpr int ATT_POLY_GROUPS = 2;  // of the 8 four-column groups of a 32-column score chunk
+__device__ __forceinline__ float2 ex2_poly2(float2 x)
+{
+    constexpr float SH = 12582912.0f;  // 1.5 x 2^23: x + SH holds round(x) in its low mantissa bits
+    constexpr float C0 = 1.0000001192092896f, C1 = 0.6931469440460205f, C2 = 0.24022121727466583f,
+                    C3 = 0.05550742521882057f, C4 = 0.00967546459287405f, C5 = 0.0013266978785395622f;
+    x = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+    const float2 t = add2(x, make_float2(SH, SH));
+    const float2 f = add2(x, add2(make_float2(SH, SH), make_float2(-t.x, -t.y)));  // x - round(x)
+    float2 p = fma2(f, make_float2(C5, C5), make_float2(C4, C4));
+    p = fma2(f, p, make_float2(C3, C3));
+    p = fma2(f, p, make_float2(C2, C2));
+    p = fma2(f, p, make_float2(C1, C1));
+    p = fma2(f, p, make_float2(C0, C0));
+    const int nx = __float_as_int(t.x) - __float_as_int(SH), ny = __float_as_int(t.y) - __float_as_int(SH);
+    return make_float2(__int_as_float(__float_as_int(p.x) + (nx << 23)), __int_as_float(__float_as_int(p.y) + (ny << 23)));
+}
+
 // Max of a row's scores in a full S buffer (TMEM, 64 columns at sS).
 __device__ __forceinline__ float tile_max(uint32_t sS)
 {
@@ -119,8 +143,14 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint32_t *w, int nvalid, f
 #pragma unroll
                 for (int e = 0; e < 4; e += 2) {
                     const float2 a = fma2(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
-                    pp[e] = ex2(a.x);
-                    pp[e + 1] = ex2(a.y);
+                    if ((i >> 2) < ATT_POLY_GROUPS) {  // this share of the exponentials on the FMA pipe
+                        const float2 q = ex2_poly2(a);
+                        pp[e] = q.x;
+                        pp[e + 1] = q.y;
+                    } else {
+                        pp[e] = ex2(a.x);
+                        pp[e + 1] = ex2(a.y);
+                    }
                     l2[e >> 1] = add2(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
                 }
                 w[c * 8 + (i >> 2)] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
