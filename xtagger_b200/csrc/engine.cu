@@ -77,6 +77,9 @@ struct Replica {
     __half *in_b = nullptr;             // input buffer 1 (buffer 0 is in)
     cudaGraphExec_t graph_b = nullptr;  // the forward reading in_b
     cudaStream_t cst = nullptr;
+    // the last query row's attention kernel runs on its own branch of the forward (fork / join events)
+    cudaStream_t ast = nullptr;
+    cudaEvent_t afork = nullptr, ajoin = nullptr;
     cudaEvent_t in_ready[2] = {}, in_free[2] = {};
     int ib = 0;                         // input buffer of the next submit
     uint32_t *errh = nullptr;           // pinned, per slot: the device error word after the slot's forward
@@ -297,7 +300,12 @@ int forward(Impl *im, Replica &r, eva *e, Prof *p)
         if (sm & 1) RCK(launch_qkv_sp(r.op_h_sp, L.sw[0], L.adq[0], rows, r.q8, r.k8, r.v8, r.cs, L.cq, L.ck, L.cv, st));
         else RCK(launch_qkv(r.op_h, L.w[0], L.adq[0], rows, r.q8, r.k8, r.v8, r.cs, L.cq, L.ck, L.cv, st));
         RCK(record(p, st, P_QKV));
-        RCK(launch_attention(r.attn, nb, r.h, L.sinv, L.vo, st));
+        // the last query row (k_attention_last) on a parallel branch: it overlaps the main attention kernel
+        ECK(cudaEventRecord(r.afork, st));
+        ECK(cudaStreamWaitEvent(r.ast, r.afork, 0));
+        RCK(launch_attention(r.attn, nb, r.h, L.sinv, L.vo, st, r.ast));
+        ECK(cudaEventRecord(r.ajoin, r.ast));
+        ECK(cudaStreamWaitEvent(st, r.ajoin, 0));
         RCK(record(p, st, P_ATTN));
         if (sm & 2) RCK(launch_oproj_sp(r.op_h_sp, L.sw[1], L.adq[1], rows, r.x, st));
         else RCK(launch_oproj(r.op_h, L.w[1], L.adq[1], rows, r.x, st));
@@ -372,6 +380,9 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     RCK(prepare_kernels());
     ECK(cudaStreamCreateWithFlags(&r.st, cudaStreamNonBlocking));
     ECK(cudaStreamCreateWithFlags(&r.cst, cudaStreamNonBlocking));
+    ECK(cudaStreamCreateWithFlags(&r.ast, cudaStreamNonBlocking));
+    ECK(cudaEventCreateWithFlags(&r.afork, cudaEventDisableTiming));
+    ECK(cudaEventCreateWithFlags(&r.ajoin, cudaEventDisableTiming));
     ECK(cudaMalloc(&r.wts, im->wbytes));
     ECK(cudaMemcpyAsync(r.wts, hostblob, im->wbytes, cudaMemcpyHostToDevice, r.st));
     int off = layout(im, r, hostblob);
@@ -875,6 +886,7 @@ void eva_close(eva *e)
         if (cudaSetDevice(r.dev) != cudaSuccess) continue;
         if (r.st) cudaStreamSynchronize(r.st);
         if (r.cst) cudaStreamSynchronize(r.cst);
+        if (r.ast) cudaStreamSynchronize(r.ast);
         if (r.graph) cudaGraphExecDestroy(r.graph);
         if (r.graph_b) cudaGraphExecDestroy(r.graph_b);
         for (int s = 0; s < EVA_NBUF; s++)
@@ -893,8 +905,11 @@ void eva_close(eva *e)
             cudaFree(r.hb);
             if (im->head8) cudaFree(r.hws);
         }
+        if (r.afork) cudaEventDestroy(r.afork);
+        if (r.ajoin) cudaEventDestroy(r.ajoin);
         if (r.st) cudaStreamDestroy(r.st);
         if (r.cst) cudaStreamDestroy(r.cst);
+        if (r.ast) cudaStreamDestroy(r.ast);
     }
     for (int s = 0; s < EVA_NBUF; s++) {
         if (im->out_reg) {

@@ -282,13 +282,13 @@ int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, 
     return 0;
 }
 
-int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st)
+int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st, cudaStream_t st_last)
 {
     if (set_smem((const void *)k_attention<AttEva>, ATT_SMEM)) return -1;
     dim3 grid(AttEva::PAIRS, NH, nimg);
     k_attention<AttEva><<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
     XTB_CK(cudaGetLastError());
-    k_attention_last<<<nimg * NH, ATT_LAST_THREADS, 0, st>>>(a.q8, a.k8, a.v8, out, sinv, vo);
+    k_attention_last<<<nimg * NH, ATT_LAST_THREADS, 0, st_last ? st_last : st>>>(a.q8, a.k8, a.v8, out, sinv, vo);
     XTB_CK(cudaGetLastError());
     return 0;
 }

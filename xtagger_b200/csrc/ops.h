@@ -61,7 +61,10 @@ int launch_ln_e4m3(const __half *x, const float *g, const float *b, uint8_t *y, 
 int launch_qkv(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *q8, uint8_t *k8, uint8_t *v8,
                const float *cs, float cq, float ck, float cv, cudaStream_t st);
 int make_attn(Attn *a, const uint8_t *q8, const uint8_t *k8, const uint8_t *v8, int nimg);
-int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st);
+// st_last: the stream of the last query row's kernel (independent of the main kernel: both read q8 / k8 / v8 and
+// write disjoint rows of out); st when null
+int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo, cudaStream_t st,
+                     cudaStream_t st_last = nullptr);
 int launch_oproj(const Operand &a, const Weight8 &w, float ascale, int rows, __half *x, cudaStream_t st);
 int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
                cudaStream_t st);
