@@ -238,3 +238,36 @@ def test_head_put_fp8_head(xlib, cuda, models):
     finally:
         eng.close()
     np.testing.assert_array_equal(again[:, 3], base[:, 3])
+
+
+def test_full_size_batch_invariance(xlib, cuda, tmp_path_factory):
+    """Config 3 at full size (the bench's 24-layer model with power-of-two block scales, batch 64): an image's
+    scores do not depend on its batch neighbours or the batch size (bit-identical at positions 5 and 63 of a batch
+    of 64 and alone), and image 0 matches the oracle within the tiling noise floor."""
+    from oracle import oracle as O
+    from xtagger_b200 import model as M
+    from xtagger_b200.engine import Engine
+    d = str(tmp_path_factory.mktemp("full"))
+    path = M.cached_synthetic(d, seed=0, nt=10861, nl=24, version=4, head_fp8=True, pow2=True)
+    x = M.synthetic_inputs(64, seed=1)
+    x[63] = x[5]
+    eng = Engine(path, nb=64)
+    try:
+        got = eng.run(x)
+        assert eng.block_scale_kinds() == 5
+    finally:
+        eng.close()
+    one = Engine(path, nb=1)
+    try:
+        alone = one.run(x[5:6])
+    finally:
+        one.close()
+    assert xlib.xtb_error_word(0) == 0
+    assert np.isfinite(got).all()
+    assert np.array_equal(got[63], got[5])
+    assert np.array_equal(alone[0], got[5])
+    want = O.forward(path, x[:1])
+    alt = O.forward(path, x[:1], key_tile=128, slice_rows=1)
+    floor = float(np.abs(alt - want).max())
+    err = float(np.abs(got[:1] - want).max())
+    assert err <= max(2e-3, 1.5 * floor), f"image 0: {err:.3e} against floor {floor:.3e}"

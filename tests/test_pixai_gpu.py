@@ -105,3 +105,32 @@ def test_px_fc1_gelu(xlib, cuda, O):
                            G.P(out), None) == 0
     G.check_error_word(xlib)
     G.assert_e4m3_close(G.host(out), want, 1, 0.99, "px fc1")
+
+
+def test_px_full_model_batch_invariance(xlib, cuda, O, tmp_path_factory):
+    """The full PixAI model (32 blocks, 30877 tags) at batch 8: bit-identical scores for the same image at two batch
+    positions and alone, and image 0 against the oracle within its tiling noise floor."""
+    from xtagger_b200 import pixai as P
+    from xtagger_b200.pxengine import PxEngine
+    d = str(tmp_path_factory.mktemp("pxfull"))
+    path = P.cached_synthetic(d, seed=0, nt=30877)
+    x = P.synthetic_inputs(8, seed=1)
+    x[7] = x[2]
+    eng = PxEngine(path, nb=8)
+    try:
+        got = eng.run(x)
+    finally:
+        eng.close()
+    one = PxEngine(path, nb=1)
+    try:
+        alone = one.run(x[2:3])
+    finally:
+        one.close()
+    assert xlib.xtb_error_word(0) == 0
+    assert np.isfinite(got).all()
+    assert np.array_equal(got[7], got[2]) and np.array_equal(alone[0], got[2])
+    want = O.px_forward(path, x[:1])
+    alt = O.px_forward(path, x[:1], key_tile=128, slice_rows=1)
+    floor = float(np.abs(alt - want).max())
+    err = float(np.abs(got[:1] - want).max())
+    assert err <= max(2e-3, 1.5 * floor), f"image 0: {err:.3e} against floor {floor:.3e}"
