@@ -222,3 +222,44 @@ extern "C" int ref_px_forward(const char *path, const uint16_t *in, int nimg, fl
     release(&B, &m);
     return rc;
 }
+
+// Device time of the reference's PixAI forward for nimg inputs already on the device: the forward captured into a
+// CUDA graph as px_up does (px.h:331-336), CUDA events around iters graph launches after warmup launches; *ms =
+// milliseconds per forward.
+extern "C" int ref_px_forward_time(const char *path, const uint16_t *in, int nimg, int warmup, int iters, float *ms)
+{
+    PModel m;
+    PBufs B;
+    int rc = -1;
+    cudaStream_t st = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (nimg > 0 && (nimg & 1) == 0 && iters > 0 && !load(path, &m) && !alloc(&B, m, nimg) &&
+        cudaStreamCreate(&st) == cudaSuccess && cudaEventCreate(&e0) == cudaSuccess &&
+        cudaEventCreate(&e1) == cudaSuccess &&
+        cudaMemcpy(B.in, in, (size_t)nimg * T * K0P * 2, cudaMemcpyHostToDevice) == cudaSuccess &&
+        cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        const int frc = forward(m, B, st);
+        if (cudaStreamEndCapture(st, &g) == cudaSuccess && !frc && cudaGraphInstantiate(&ge, g, 0) == cudaSuccess) {
+            bool ok = true;
+            for (int i = 0; i < warmup && ok; i++) ok = cudaGraphLaunch(ge, st) == cudaSuccess;
+            ok = ok && cudaEventRecord(e0, st) == cudaSuccess;
+            for (int i = 0; i < iters && ok; i++) ok = cudaGraphLaunch(ge, st) == cudaSuccess;
+            ok = ok && cudaEventRecord(e1, st) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess;
+            float t = 0.f;
+            if (ok && cudaEventElapsedTime(&t, e0, e1) == cudaSuccess) {
+                *ms = t / iters;
+                rc = 0;
+            }
+        }
+    }
+    if (rc) fprintf(stderr, "ref_px: ref_px_forward_time failed: %s\n", cudaGetErrorString(cudaGetLastError()));
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    if (st) cudaStreamDestroy(st);
+    release(&B, &m);
+    return rc;
+}

@@ -6,6 +6,7 @@ graph as the reference does; CUDA events around `iters` graph launches after `wa
 batch size: images/s with inputs resident on the device, the same measurement bench.py's `value` makes.
 
     python oracle/ref_time.py [--batch 8 64] [--iters 10] [--warmup 3]
+    python oracle/ref_time.py --pixai [--batch 4 8]    # the reference's PixAI forward (px_kernels.cu, px.h:115-190)
 """
 import argparse
 import ctypes as C
@@ -25,8 +26,12 @@ def main():
     ap.add_argument("--batch", type=int, nargs="+", default=[8, 64])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--nt", type=int, default=10861)
+    ap.add_argument("--nt", type=int, default=None)
+    ap.add_argument("--pixai", action="store_true", help="the PixAI forward (full 32-block model, 30877 tags)")
     a = ap.parse_args()
+    if a.pixai:
+        return pixai(a)
+    a.nt = a.nt or 10861
     from xtagger_b200 import model as M
     lib = C.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so"))
     lib.ref_forward_time.restype = C.c_int
@@ -42,6 +47,24 @@ def main():
         print(json.dumps({"impl": "reference kernels (eva_kernels.cu, mma.sync E4M3) on this GPU", "batch": nb,
                           "ms_per_forward": ms.value, "images_per_s": nb / (ms.value * 1e-3),
                           "model": f"v3, 24 layers, fp16 head, {a.nt} tags, random-init"}), flush=True)
+
+
+def pixai(a):
+    from xtagger_b200 import pixai as P
+    lib = C.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_px.so"))
+    lib.ref_px_forward_time.restype = C.c_int
+    lib.ref_px_forward_time.argtypes = [C.c_char_p, np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS"), C.c_int,
+                                        C.c_int, C.c_int, C.POINTER(C.c_float)]
+    nt = a.nt or 30877
+    path = P.write_synthetic(os.path.join(tempfile.mkdtemp(), "px.bin"), seed=0, nt=nt)
+    for nb in a.batch:
+        x = np.ascontiguousarray(P.synthetic_inputs(nb, seed=1))
+        ms = C.c_float(0)
+        if lib.ref_px_forward_time(path.encode(), x, nb, a.warmup, a.iters, C.byref(ms)):
+            raise SystemExit("reference PixAI forward failed")
+        print(json.dumps({"impl": "reference PixAI kernels (px_kernels.cu, mma.sync E4M3) on this GPU", "batch": nb,
+                          "ms_per_forward": ms.value, "images_per_s": nb / (ms.value * 1e-3),
+                          "model": f"pixai.bin v3, 32 blocks, {nt} tags, random-init"}), flush=True)
 
 
 if __name__ == "__main__":
