@@ -54,3 +54,35 @@ def test_gemm_blockscaled_matches_fp32(xlib, cuda, m, n, k):
     assert err.max().item() <= 1e-2 * scale, (err.max().item(), scale)
     # elementwise: relative 1e-2 with a floor at 1e-3 of the output range
     assert bool((err <= 1e-2 * ref.abs() + 1e-3 * scale).all())
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("m,n,k", [(2050, 5472, 1024), (1000, 1024, 2736), (300, 3072, 1024)])
+def test_gemm_block_scale_mma(xlib, cuda, m, n, k, pair):
+    """The block-scaled MMA kernels (single CTA and CTA pair) against the oracle's dequantize-then-matmul on
+    power-of-two block scales that vary across N and K blocks: the same sums up to the fp32 order."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    from xtagger_b200 import model as M
+    from tests import _gpu as G
+    rng = np.random.default_rng(m + n + k + pair)
+    a = O.e4m3(rng.standard_normal((m, k), dtype=np.float32) * 40)
+    w = rng.standard_normal((n, k), dtype=np.float32) * 0.02
+    w[:, : k // 3] *= 16.0
+    w[n // 2:] *= 0.125
+    wq, ws = M.quant_blocks(w, pow2=True)
+    assert len(np.unique(ws)) > 2
+    img = np.zeros(xlib.xtb_sf_image_bytes(n, k), np.uint8)
+    assert xlib.xtb_sf_image(ws.ctypes.data_as(C.c_void_p), n, k, img.ctypes.data_as(C.c_void_p)) == 0
+    ascale = 1.0 / 40
+    want = O.gemm_e4m3(a, wq, ws, ascale)
+    out = G.zeros((m, n), torch.float32)
+    assert xlib.xtb_gemm_mx_f32(G.P(G.dev(a)), m, k, G.P(G.dev(wq)), n, G.P(G.dev(img)), pair, ascale, G.P(out), n,
+                                None) == 0
+    G.check_error_word(xlib)
+    got = G.host(out)
+    scale = np.abs(want).max()
+    err = np.abs(got - want)
+    assert err.max() <= 1e-5 * scale, (err.max(), scale)

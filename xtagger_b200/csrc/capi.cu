@@ -119,6 +119,24 @@ int xtb_sf_image(const float *ws, int n, int k, uint8_t *img)
     return sf_image(ws, n, k, img);
 }
 
+int xtb_gemm_mx_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, const uint8_t *sf, int pair, float ascale,
+                    float *out, int ldo, void *stream)
+{
+    Operand A;
+    Weight8 W;
+    if (!rows_ok(m, "xtb_gemm_mx_f32") || !sf || n <= 0 || k <= 0 || (k & 15) || ldo < n ||
+        make_operand(&A, a, m, k, 128) || make_operand(&W.op, w, n, k, pair ? 64 : 256))
+        return -1;
+    W.ws = nullptr;
+    W.n = n;
+    W.k = k;
+    W.sf = sf;
+    W.sf_nbp = (((n + 127) / 128) + 1) & ~1;
+    W.sf_pair = pair != 0;
+    if (W.sf_pair && sf_map(&W.sfmap, sf, n, k)) return -1;
+    return launch_gemm_f32(A, W, ascale, out, ldo, S(stream));
+}
+
 int xtb_fc1_mx(const uint8_t *h, int rows, const uint8_t *w, const uint8_t *sf, float ascale, uint8_t *h8, float *stat,
                const float *rs, void *stream)
 {

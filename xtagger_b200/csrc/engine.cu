@@ -395,7 +395,12 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
         // the four, QKV and fc1 (bits 0, 2): measured in the batch-64 forward, QKV 5.3 against 7.0 ms and fc1 8.2
         // against 10.9 ms, while the out-projection is even (2.2 ms) and fc2 is faster on the promoting CTA-pair
         // kernel (5.5 against 6.6 ms: its A operand streams from DRAM, and the pair's deeper ring feeds it better)
-        constexpr int kMxKinds = 0x5;
+        // the CTA-pair block-scaled kernel (gemm2_mx.cuh, 256 x 128 tiles) for the kinds in kMxPair: fc2, whose A
+        // operand streams from DRAM and wants the pair's halved B feed. XTB_MX_KINDS / XTB_MX_PAIR (hex masks) in the
+        // environment override both for measurements.
+        int kMxKinds = 0xD, kMxPair = 0x8;
+        if (const char *m = getenv("XTB_MX_KINDS")) kMxKinds = (int)strtol(m, nullptr, 16);
+        if (const char *m = getenv("XTB_MX_PAIR")) kMxPair = (int)strtol(m, nullptr, 16);
         const char *env = getenv("XTB_MX");
         if (!(env && env[0] == '0')) {
             size_t per[NG], off[NG], total = 0;
@@ -427,7 +432,10 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
                         Weight8 &w = r.L[i].w[g];
                         w.sf = r.sfimg + off[g] + (size_t)i * per[g];
                         w.sf_nbp = ((w.n + 127) / 128 + 1) & ~1;
-                        RCK(make_operand(&w.op, w.op.ptr, w.n, w.k, 256));  // the block-scaled kernel's 256-row boxes
+                        w.sf_pair = (kMxPair >> g) & 1;
+                        // the block-scaled kernels' B boxes: 256 rows (one CTA) or 64 per CTA (pair)
+                        RCK(make_operand(&w.op, w.op.ptr, w.n, w.k, w.sf_pair ? 64 : 256));
+                        if (w.sf_pair) RCK(sf_map(&w.sfmap, w.sf, w.n, w.k));
                     }
                 }
             }

@@ -5,6 +5,7 @@
 #include "attention.cuh"
 #include "epilogues.cuh"
 #include "gemm.cuh"
+#include "gemm2_mx.cuh"
 #include "gemm_mx.cuh"
 #include "gemm_sp.cuh"
 #include "host.h"
@@ -142,6 +143,45 @@ int sf_image(const float *ws, int n, int k, uint8_t *img)
     return 0;
 }
 
+int sf_map(CUtensorMap *m, const uint8_t *sf, int n, int k)
+{
+    const uint64_t rows = (uint64_t)kb(k) * ((kb(n) + 1) & ~1) * 2;
+    return make_tmap_2d(m, sf, 256, rows, 256, 256, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// One launch of the CTA-pair block-scaled GEMM (power-of-two block scales, w.sf, w.sfmap): 256 x 128 tiles.
+template <class Epi>
+static int run_gemm2_mx(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep,
+                        cudaStream_t st, const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
+{
+    using Cfg = Gemm2MxCfg<StagingOf<Epi>::v>;
+    auto kern = k_gemm2_mx<Epi>;
+    if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
+    if (!w.sf || a.row_bytes != w.op.row_bytes || M <= 0 || a.box_rows != A_BOX_ROWS || w.op.box_rows != Cfg::BN / 2) {
+        fprintf(stderr, "eva: pair mx gemm operands (scale image %p, K bytes %d vs %d, boxes %d / %d rows, M %d)\n",
+                (const void *)w.sf, a.row_bytes, w.op.row_bytes, a.box_rows, w.op.box_rows, M);
+        return -1;
+    }
+    const int dev = current_device();
+    GemmArgs g{};
+    g.M = M;
+    g.N = w.n;
+    g.kiters = (a.row_bytes + 127) / 128;
+    g.m_tiles = (M + 255) / 256;
+    g.n_tiles = (w.n + Cfg::BN - 1) / Cfg::BN;
+    g.ascale = ascale;
+    g.wsu = 1.0f;
+    g.err = err ? err : error_word(dev);
+    GemmMxArgs mx{w.sf, w.sf_nbp};
+    const int total = g.m_tiles * g.n_tiles;
+    int pairs = max_pairs((const void *)kern, Cfg::THREADS, Cfg::SMEM);
+    if (pairs <= 0) return -1;
+    if (pairs > total) pairs = total;
+    kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, w.op.map, w.sfmap, tmc ? *tmc : a.map, g, mx, ep);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
 // One launch of the block-scaled GEMM on the tensor core's own scaling (power-of-two block scales, w.sf).
 template <class Epi>
 static int run_gemm_mx(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep,
@@ -196,7 +236,9 @@ template <class Epi, WeightUse U>
 static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep, cudaStream_t st,
                     const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
 {
-    if (w.sf) return run_gemm_mx<Epi>(a, w, M, ascale, ep, st, tmc, err);  // power-of-two block scales
+    if (w.sf)  // power-of-two block scales
+        return w.sf_pair ? run_gemm2_mx<Epi>(a, w, M, ascale, ep, st, tmc, err)
+                         : run_gemm_mx<Epi>(a, w, M, ascale, ep, st, tmc, err);
     if (!kPairG[U] && w.uniform > 0.0f) {  // one scale for the whole weight: accumulate over K in TMEM, scale once
         if constexpr (kPair[U])
             return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
@@ -517,6 +559,14 @@ int prepare_kernels()
         set_smem((const void *)k_gemm_mx<EpiResid>, GemmMxCfg<StagingOf<EpiResid>::v>::SMEM) ||
         set_smem((const void *)k_gemm_mx<EpiFC2>, GemmMxCfg<StagingOf<EpiFC2>::v>::SMEM))
         return -1;
+    {
+        const void *k2[] = {(const void *)k_gemm2_mx<EpiQKV>, (const void *)k_gemm2_mx<EpiFC1>,
+                            (const void *)k_gemm2_mx<EpiFC2>, (const void *)k_gemm2_mx<EpiResid>};
+        const size_t sm2[] = {Gemm2MxCfg<StagingOf<EpiQKV>::v>::SMEM, Gemm2MxCfg<StagingOf<EpiFC1>::v>::SMEM,
+                              Gemm2MxCfg<StagingOf<EpiFC2>::v>::SMEM, Gemm2MxCfg<StagingOf<EpiResid>::v>::SMEM};
+        for (int i = 0; i < 4; i++)
+            if (set_smem(k2[i], sm2[i]) || max_pairs(k2[i], 320, sm2[i]) <= 0) return -1;
+    }
     return 0;
 }
 

@@ -43,7 +43,12 @@ struct Weight8 {
     // exponent repeated) for the tensor core's own block scaling (gemm_mx.cuh); null otherwise
     const uint8_t *sf = nullptr;
     int sf_nbp = 0;
+    // run on the CTA-pair block-scaled kernel (gemm2_mx.cuh: the operand op in 64-row boxes, sfmap over sf)
+    bool sf_pair = false;
+    CUtensorMap sfmap;
 };
+// The scale-factor image as the pair kernel's tensor map (512-byte records as 2 rows of 256 bytes).
+int sf_map(CUtensorMap *m, const uint8_t *sf, int n, int k);
 // Scale-factor image of block scales ws [ceil(n/128)][ceil(k/128)] (host memory) into img (sf_image_bytes(n, k)
 // bytes): 0 if every scale is a power of two (a normal float with a zero mantissa), else -1 and img untouched.
 size_t sf_image_bytes(int n, int k);

@@ -377,6 +377,21 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
+// Pair forms of the block-scaled MMA (issued by rank 0) and of the scale-factor copy into tensor memory (issued by
+// rank 0 for both CTAs of the pair).
+__device__ __forceinline__ void umma_pair_mx(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                             uint32_t sfb, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_cp_pair_32x128b_x4(uint32_t taddr, uint64_t sdesc_)
+{
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc_) : "memory");
+}
 // Pair MMA (issued by rank 0 for both CTAs), E4M3 x E4M3 -> f32: A rows from each CTA's own shared memory, B rows
 // from both, D rows of each CTA in its own TMEM; descriptors give the (identical) shared-memory offsets.
 __device__ __forceinline__ void umma_pair_e4m3(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
@@ -453,6 +468,11 @@ __host__ __device__ constexpr uint32_t idesc_m128(uint32_t n)
 __host__ __device__ constexpr uint32_t idesc_mx_m128(uint32_t n, uint32_t sfa_id, uint32_t sfb_id)
 {
     return ((sfb_id & 3u) << 4) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) | ((sfa_id & 3u) << 29);
+}
+// The same for a CTA-pair MMA of M = 256.
+__host__ __device__ constexpr uint32_t idesc_mx_m256(uint32_t n, uint32_t sfa_id, uint32_t sfb_id)
+{
+    return ((sfb_id & 3u) << 4) | ((n >> 3) << 17) | (1u << 23) | ((256u >> 4) << 24) | ((sfa_id & 3u) << 29);
 }
 // The same with A 2:4-sparse (bit 2; K = 64 logical elements per instruction).
 __host__ __device__ constexpr uint32_t idesc_sp_m128(uint32_t n) { return idesc_m128(n) | (1u << 2); }

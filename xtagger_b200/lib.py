@@ -93,6 +93,7 @@ _SIGS = {
     "xtb_sf_image_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "xtb_sf_image": (C.c_int, [_P, C.c_int, C.c_int, _P]),
     "xtb_fc1_mx": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P]),
+    "xtb_gemm_mx_f32": (C.c_int, [_P, C.c_int, C.c_int, _P, C.c_int, _P, C.c_int, C.c_float, _P, C.c_int, _P]),
     "xtb_fc2": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
     "xtb_patch_embed": (C.c_int, [_P, C.c_int, _P, _P, _P, _P]),
     "xtb_pool_ln": (C.c_int, [_P, C.c_int, _P, _P, _P, _P, _P, C.c_float, _P]),
