@@ -64,7 +64,7 @@ def test_forward_matches_oracle(xlib, cuda, models, name, nimg):
         try:
             got = eng.run(x)
             assert eng.sparse_kinds() == (15 if name.endswith("_p") else 0)
-            assert eng.block_scale_kinds() == (13 if name.endswith("_pow2") else 0)
+            assert eng.block_scale_kinds() == (7 if name.endswith("_pow2") else 0)
         finally:
             eng.close()
     finally:
@@ -254,7 +254,7 @@ def test_full_size_batch_invariance(xlib, cuda, tmp_path_factory):
     eng = Engine(path, nb=64)
     try:
         got = eng.run(x)
-        assert eng.block_scale_kinds() == 13
+        assert eng.block_scale_kinds() == 7
     finally:
         eng.close()
     one = Engine(path, nb=1)

@@ -391,14 +391,14 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
     if (!im->sp_ready) RCK(sparse_prepare(im, r, hostblob));
     if (im->ver == 4 && !im->sp_mask) {
         // projection kinds whose block scales are all powers of two, in every layer, run on the tensor core's own
-        // block scaling (no per-K-block promotion); XTB_MX=0 in the environment keeps the promoting kernels. Of
-        // the four, QKV and fc1 (bits 0, 2): measured in the batch-64 forward, QKV 5.3 against 7.0 ms and fc1 8.2
-        // against 10.9 ms, while the out-projection is even (2.2 ms) and fc2 is faster on the promoting CTA-pair
-        // kernel (5.5 against 6.6 ms: its A operand streams from DRAM, and the pair's deeper ring feeds it better)
-        // the CTA-pair block-scaled kernel (gemm2_mx.cuh, 256 x 128 tiles) for the kinds in kMxPair: fc2, whose A
-        // operand streams from DRAM and wants the pair's halved B feed. XTB_MX_KINDS / XTB_MX_PAIR (hex masks) in the
-        // environment override both for measurements.
-        int kMxKinds = 0xD, kMxPair = 0x8;
+        // block scaling (no per-K-block promotion); XTB_MX=0 in the environment keeps the promoting kernels
+        // (promoting, the batch-64 forward spends 7.0 ms in QKV and 10.9 in fc1)
+        // the CTA-pair block-scaled kernel (gemm2_mx.cuh, 256 x 128 tiles) for the kinds in kMxPair. Measured in the
+        // batch-64 forward (power-capped clocks): QKV 5.2 ms on the pair against 5.3 on one CTA, the out-projection
+        // 1.9 against 2.4 promoting, fc1 8.1 on one CTA against 8.25 on the pair; fc2 stays on the promoting CTA pair
+        // (6.0 ms; 6.5 on the block-scaled pair, whose 128-column tiles double its B traffic per FLOP).
+        // XTB_MX_KINDS / XTB_MX_PAIR (hex masks) in the environment override both for measurements.
+        int kMxKinds = 0x7, kMxPair = 0x3;
         if (const char *m = getenv("XTB_MX_KINDS")) kMxKinds = (int)strtol(m, nullptr, 16);
         if (const char *m = getenv("XTB_MX_PAIR")) kMxPair = (int)strtol(m, nullptr, 16);
         const char *env = getenv("XTB_MX");
