@@ -115,8 +115,38 @@ __device__ __forceinline__ float tile_max(uint32_t sS)
     return fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
 }
 
+// Columns [16 cc, 16 cc + 16) of a full score row (v, 16 values) into the pass's accumulators: the same operations
+// in the same order as the 32-column loop of exp_pass below (tile max per 4-column half, exponent, l, E4M3 pairs).
+__device__ __forceinline__ void exp_cols16(const float *v, int cc, float2 sv2, float2 nm2, float *t4, float2 *l2,
+                                           uint32_t *w)
+{
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+        const int g = (cc & 1) * 16 + i;  // column within the 32-column chunk
+        t4[(i >> 2) & 1] = fmax3(t4[(i >> 2) & 1], v[i], v[i + 1]);
+        t4[2 + ((i >> 2) & 1)] = fmax3(t4[2 + ((i >> 2) & 1)], v[i + 2], v[i + 3]);
+        float pp[4];
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+            const float2 a = fma2(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
+            if ((g >> 2) < ATT_POLY_GROUPS) {
+                const float2 q = ex2_poly2(a);
+                pp[e] = q.x;
+                pp[e + 1] = q.y;
+            } else {
+                pp[e] = ex2(a.x);
+                pp[e + 1] = ex2(a.y);
+            }
+            l2[e >> 1] = add2(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
+        }
+        w[cc * 4 + (i >> 2)] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
+    }
+}
+
 // One pass over a row of an S buffer with max m: tile max, p = exp2(s sinv - m sinv), sum of p, E4M3(p) -> the
 // row of P. FULL: all 64 keys are valid (every step but the last); otherwise keys >= nvalid are masked (p = 0).
+// The full pass reads the row in four 16-column loads, each issued before the math on the previous one, so that
+// only the first load's latency is exposed; the results are those of the 32-column loop (same order of operations).
 template <bool FULL>
 __device__ __forceinline__ void exp_pass(uint32_t sS, uint32_t *w, int nvalid, float2 sv2, float m, float *tm_out,
                                          float *l_out)
@@ -124,6 +154,22 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint32_t *w, int nvalid, f
     const float2 nm2 = make_float2(-m * sv2.x, -m * sv2.x);
     float t4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     float2 l2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    if constexpr (FULL) {
+        float va[16], vb[16];
+        tmem_ld16(sS, va);
+        tmem_wait_ld_regs16(va);
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) {
+            float *cur = (cc & 1) ? vb : va;
+            float *nxt = (cc & 1) ? va : vb;
+            if (cc < 3) tmem_ld16(sS + (cc + 1) * 16, nxt);
+            exp_cols16(cur, cc, sv2, nm2, t4, l2, w);
+            if (cc < 3) tmem_wait_ld_regs16(nxt);
+        }
+        *tm_out = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
+        *l_out = (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
+        return;
+    }
 #pragma unroll
     for (int c = 0; c < 2; c++) {
         if (FULL || c * 32 < nvalid) {  // warp-uniform
