@@ -195,8 +195,8 @@ int xtb_sf_image(const float *ws, int n, int k, uint8_t *img);
 int xtb_fc1_mx(const uint8_t *h, int rows, const uint8_t *w, const uint8_t *sf, float ascale, uint8_t *h8, float *stat,
                const float *rs, void *stream);
 /* out[m][n] (fp32, row stride ldo) = ascale * A W^T on the block-scaled MMA: A E4M3 [m][k], W E4M3 [n][k] with its
- * scale-factor image sf (xtb_sf_image); pair != 0 runs the CTA-pair kernel (256 x 128 tiles), else the single-CTA
- * one (128 x 256). k a multiple of 16. */
+ * scale-factor image sf (xtb_sf_image); pair = 1 runs the CTA-pair kernel (256 x 128 tiles), pair = 2 the CTA pair
+ * on 256 x 256 tiles (two weight blocks per tile), pair = 0 the single-CTA one (128 x 256). k a multiple of 16. */
 int xtb_gemm_mx_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, const uint8_t *sf, int pair, float ascale,
                     float *out, int ldo, void *stream);
 /* As xtb_qkv / xtb_oproj / xtb_fc1 / xtb_fc2 with the weight compressed (vals, meta) and its block scales ws. */

@@ -56,11 +56,12 @@ def test_gemm_blockscaled_matches_fp32(xlib, cuda, m, n, k):
     assert bool((err <= 1e-2 * ref.abs() + 1e-3 * scale).all())
 
 
-@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("pair", [0, 1, 2])
 @pytest.mark.parametrize("m,n,k", [(2050, 5472, 1024), (1000, 1024, 2736), (300, 3072, 1024)])
 def test_gemm_block_scale_mma(xlib, cuda, m, n, k, pair):
-    """The block-scaled MMA kernels (single CTA and CTA pair) against the oracle's dequantize-then-matmul on
-    power-of-two block scales that vary across N and K blocks: the same sums up to the fp32 order."""
+    """The block-scaled MMA kernels (single CTA, CTA pair, CTA pair on 256-column tiles) against the oracle's
+    dequantize-then-matmul on power-of-two block scales that vary across N and K blocks, adjacent 128-row weight
+    blocks included (a wide tile spans two): the same sums up to the fp32 order."""
     import ctypes as C
     import numpy as np
     import torch
@@ -72,7 +73,9 @@ def test_gemm_block_scale_mma(xlib, cuda, m, n, k, pair):
     w = rng.standard_normal((n, k), dtype=np.float32) * 0.02
     w[:, : k // 3] *= 16.0
     w[n // 2:] *= 0.125
+    w[(np.arange(n) // 128) % 2 == 1] *= 4.0    # odd weight blocks four times their neighbours
     wq, ws = M.quant_blocks(w, pow2=True)
+    assert np.all(ws[1::2, 0][: (n // 128) // 2] != ws[0::2, 0][: (n // 128) // 2])
     assert len(np.unique(ws)) > 2
     img = np.zeros(xlib.xtb_sf_image_bytes(n, k), np.uint8)
     assert xlib.xtb_sf_image(ws.ctypes.data_as(C.c_void_p), n, k, img.ctypes.data_as(C.c_void_p)) == 0

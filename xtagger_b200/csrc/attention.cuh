@@ -166,44 +166,40 @@ __device__ __forceinline__ void exp_pass(uint32_t sS, uint32_t *w, int nvalid, f
             exp_cols16(cur, cc, sv2, nm2, t4, l2, w);
             if (cc < 3) tmem_wait_ld_regs16(nxt);
         }
-        *tm_out = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));
-        *l_out = (l2[0].x + l2[0].y) + (l2[1].x + l2[1].y);
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
-        if (FULL || c * 32 < nvalid) {  // warp-uniform
-            float v[32];
-            tmem_ld32(sS + c * 32, v);
-            tmem_wait_ld();
-            if (!FULL) {
+        for (int c = 0; c < 2; c++) {
+            if (c * 32 < nvalid) {  // warp-uniform
+                float v[32];
+                tmem_ld32(sS + c * 32, v);
+                tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i++)
                     if (c * 32 + i >= nvalid) v[i] = -INFINITY;
-            }
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-                t4[(i >> 2) & 1] = fmax3(t4[(i >> 2) & 1], v[i], v[i + 1]);
-                t4[2 + ((i >> 2) & 1)] = fmax3(t4[2 + ((i >> 2) & 1)], v[i + 2], v[i + 3]);
-                float pp[4];
+                for (int i = 0; i < 32; i += 4) {
+                    t4[(i >> 2) & 1] = fmax3(t4[(i >> 2) & 1], v[i], v[i + 1]);
+                    t4[2 + ((i >> 2) & 1)] = fmax3(t4[2 + ((i >> 2) & 1)], v[i + 2], v[i + 3]);
+                    float pp[4];
 #pragma unroll
-                for (int e = 0; e < 4; e += 2) {
-                    const float2 a = fma2(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
-                    if ((i >> 2) < ATT_POLY_GROUPS) {  // this share of the exponentials on the FMA pipe
-                        const float2 q = ex2_poly2(a);
-                        pp[e] = q.x;
-                        pp[e + 1] = q.y;
-                    } else {
-                        pp[e] = ex2(a.x);
-                        pp[e + 1] = ex2(a.y);
+                    for (int e = 0; e < 4; e += 2) {
+                        const float2 a = fma2(make_float2(v[i + e], v[i + e + 1]), sv2, nm2);
+                        if ((i >> 2) < ATT_POLY_GROUPS) {  // this share of the exponentials on the FMA pipe
+                            const float2 q = ex2_poly2(a);
+                            pp[e] = q.x;
+                            pp[e + 1] = q.y;
+                        } else {
+                            pp[e] = ex2(a.x);
+                            pp[e + 1] = ex2(a.y);
+                        }
+                        l2[e >> 1] = add2(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
                     }
-                    l2[e >> 1] = add2(l2[e >> 1], make_float2(pp[e], pp[e + 1]));
+                    w[c * 8 + (i >> 2)] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
                 }
-                w[c * 8 + (i >> 2)] = e4m3x2(pp[0], pp[1]) | (e4m3x2(pp[2], pp[3]) << 16);
-            }
-        } else {
+            } else {
 #pragma unroll
-            for (int i = 0; i < 8; i++) w[c * 8 + i] = 0;
+                for (int i = 0; i < 8; i++) w[c * 8 + i] = 0;
+            }
         }
     }
     *tm_out = fmaxf(fmaxf(t4[0], t4[1]), fmaxf(t4[2], t4[3]));

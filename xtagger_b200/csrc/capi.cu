@@ -125,7 +125,7 @@ int xtb_gemm_mx_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, con
     Operand A;
     Weight8 W;
     if (!rows_ok(m, "xtb_gemm_mx_f32") || !sf || n <= 0 || k <= 0 || (k & 15) || ldo < n ||
-        make_operand(&A, a, m, k, 128) || make_operand(&W.op, w, n, k, pair ? 64 : 256))
+        pair < 0 || pair > 2 || make_operand(&A, a, m, k, 128) || make_operand(&W.op, w, n, k, pair ? 64 : 256))
         return -1;
     W.ws = nullptr;
     W.n = n;
@@ -133,6 +133,7 @@ int xtb_gemm_mx_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, con
     W.sf = sf;
     W.sf_nbp = (((n + 127) / 128) + 1) & ~1;
     W.sf_pair = pair != 0;
+    W.sf_wide = pair == 2;
     if (W.sf_pair && sf_map(&W.sfmap, sf, n, k)) return -1;
     return launch_gemm_f32(A, W, ascale, out, ldo, S(stream));
 }

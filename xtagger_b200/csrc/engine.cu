@@ -393,14 +393,17 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
         // projection kinds whose block scales are all powers of two, in every layer, run on the tensor core's own
         // block scaling (no per-K-block promotion); XTB_MX=0 in the environment keeps the promoting kernels
         // (promoting, the batch-64 forward spends 7.0 ms in QKV and 10.9 in fc1)
-        // the CTA-pair block-scaled kernel (gemm2_mx.cuh, 256 x 128 tiles) for the kinds in kMxPair. Measured in the
-        // batch-64 forward (power-capped clocks): QKV 5.2 ms on the pair against 5.3 on one CTA, the out-projection
-        // 1.9 against 2.4 promoting, fc1 8.1 on one CTA against 8.25 on the pair; fc2 stays on the promoting CTA pair
-        // (6.0 ms; 6.5 on the block-scaled pair, whose 128-column tiles double its B traffic per FLOP).
-        // XTB_MX_KINDS / XTB_MX_PAIR (hex masks) in the environment override both for measurements.
-        int kMxKinds = 0x7, kMxPair = 0x3;
+        // the CTA-pair block-scaled kernel (gemm2_mx.cuh) for the kinds in kMxPair, on 256 x 256 tiles (two weight
+        // blocks per tile, half the A traffic per FLOP) for those in kMxWide (N a multiple of 256), else 256 x 128.
+        // Measured in the batch-64 forward (power-capped clocks, ms per forward): fc2 4.97 on the pair's wide tiles
+        // against 6.2 on the promoting pair and 6.5 on 128-column block-scaled tiles; QKV 4.41 wide against 4.95 on
+        // 128-column tiles and 5.3 on one CTA; the out-projection 1.86 on 128-column tiles against 1.96 wide and 2.4
+        // promoting; fc1 8.1 on one CTA against 8.25 on the pair.
+        // XTB_MX_KINDS / XTB_MX_PAIR / XTB_MX_WIDE (hex masks) in the environment override these for measurements.
+        int kMxKinds = 0xF, kMxPair = 0xB, kMxWide = 0x9;
         if (const char *m = getenv("XTB_MX_KINDS")) kMxKinds = (int)strtol(m, nullptr, 16);
         if (const char *m = getenv("XTB_MX_PAIR")) kMxPair = (int)strtol(m, nullptr, 16);
+        if (const char *m = getenv("XTB_MX_WIDE")) kMxWide = (int)strtol(m, nullptr, 16);
         const char *env = getenv("XTB_MX");
         if (!(env && env[0] == '0')) {
             size_t per[NG], off[NG], total = 0;
@@ -433,6 +436,7 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
                         w.sf = r.sfimg + off[g] + (size_t)i * per[g];
                         w.sf_nbp = ((w.n + 127) / 128 + 1) & ~1;
                         w.sf_pair = (kMxPair >> g) & 1;
+                        w.sf_wide = w.sf_pair && ((kMxWide >> g) & 1) && w.n % 256 == 0;
                         // the block-scaled kernels' B boxes: 256 rows (one CTA) or 64 per CTA (pair)
                         RCK(make_operand(&w.op, w.op.ptr, w.n, w.k, w.sf_pair ? 64 : 256));
                         if (w.sf_pair) RCK(sf_map(&w.sfmap, w.sf, w.n, w.k));

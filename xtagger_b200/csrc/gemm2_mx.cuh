@@ -13,21 +13,30 @@
 // per lane quadrant, 128 columns per thread, gemm2.cuh's GROUPS layout) take the pair's tiles in turn, each with
 // its own buffer, so one group's drain and fused apply overlap the MMA of the other group's tile; TMEM: buffers at
 // columns 0 / 128, A scale factors at 256, B scale factors at 288.
+//
+// NB2 = 2 (wide tiles): a pair computes 256 x 256 tiles as two M = 256, N = 128 MMAs per 128-byte K slice, one per
+// 128-row weight block, each with that block's own uniform scale record (B scale factors at columns 288 and 296), so
+// each A slice brought into shared memory serves 256 output columns instead of 128: half the A traffic per FLOP,
+// for projections whose A operand streams from DRAM (fc2: K = 2736). The tile's accumulator fills columns 0 .. 255,
+// so there is one buffer: epilogue group g drains columns 128 g .. 128 g + 127 of every tile, and the next tile's
+// MMAs start once both groups of both CTAs have read it.
 #pragma once
 #include "gemm2.cuh"
 #include "gemm_mx.cuh"
 
 namespace xtb {
 
-template <int SPW>
+template <int SPW, int NB2 = 1>
 struct Gemm2MxCfg {
-    static constexpr int BN = 128;
+    static_assert(NB2 == 1 || NB2 == 2, "one or two weight blocks per tile");
+    static constexpr int BN = 128 * NB2;                    // tile columns
     static constexpr int EW = 8;                            // two groups of four epilogue warps
-    static constexpr int COLS = BN;                         // accumulator columns per epilogue thread
-    static constexpr int TEMPTY = 2 * 4;                    // a group's warps in both CTAs free its buffer
+    static constexpr int COLS = 128;                        // accumulator columns per epilogue thread
+    static constexpr int NBUF = 3 - NB2;                    // accumulator buffers (one per group, or one shared)
+    static constexpr int TEMPTY = NB2 * 2 * 4;              // the buffer's readers: one or both groups, both CTAs
     static constexpr int A_BYTES = 128 * 128;
-    static constexpr int B_BYTES = (BN / 2) * 128;
-    static constexpr int SF_BYTES = 512;
+    static constexpr int B_BYTES = NB2 * 64 * 128;          // per weight block: 64 rows per CTA
+    static constexpr int SF_BYTES = NB2 * 512;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGING = EW * SPW;
     static constexpr int STAGES_FIT = (232448 - 1024 - 1024 - 1024 - 512 - STAGING) / (STAGE_BYTES + SF_BYTES);
@@ -35,17 +44,17 @@ struct Gemm2MxCfg {
     static constexpr int SF_AREA = (STAGES * SF_BYTES + 1023) & ~1023;   // keeps the staging 1024-aligned
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + SF_AREA + STAGING + 512 + 1024;
     static constexpr int THREADS = 64 + 32 * EW;
-    static constexpr uint32_t SFA_COL = 256, SFB_COL = 288;
+    static constexpr uint32_t SFA_COL = 256, SFB_COL = 288;  // weight block j's B scale factors at SFB_COL + 8 j
     static_assert(STAGES >= 4 && SMEM <= 232448, "shared memory budget");
 };
 
-template <class Epi>
+template <class Epi, int NB2 = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     k_gemm2_mx(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmSF, const __grid_constant__ CUtensorMap tmC, const GemmArgs g,
                const GemmMxArgs mx, const typename Epi::Params ep)
 {
-    using C = Gemm2MxCfg<StagingOf<Epi>::v>;
+    using C = Gemm2MxCfg<StagingOf<Epi>::v, NB2>;
     constexpr int STAGES = C::STAGES, COLS = C::COLS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -56,8 +65,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     uint8_t *sSFA = sStage + C::STAGING;                // 512 bytes of 2^0 scale factors
     uint64_t *full = (uint64_t *)(sSFA + 512);          // rank 0: both producers' bytes
     uint64_t *empty = full + STAGES;                    // every rank: stage consumed by the pair MMA
-    uint64_t *tfull = empty + STAGES;                   // every rank: [group] tile accumulated
-    uint64_t *tempty = tfull + 2;                       // rank 0: [group] buffer read by the group in both CTAs
+    uint64_t *tfull = empty + STAGES;                   // every rank: [buffer] tile accumulated
+    uint64_t *tempty = tfull + 2;                       // rank 0: [buffer] buffer read by its readers in both CTAs
     uint32_t *tslot = (uint32_t *)(tempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -105,8 +114,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                     const uint32_t fb = full0 + stage * 8;
                     mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES + C::SF_BYTES);
                     tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, fb, k * 128, mb * 256 + rank * 128);
-                    tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, fb, k * 128, nb * C::BN + rank * (C::BN / 2));
-                    tma_load_2d_pair(sSF + stage * C::SF_BYTES, &tmSF, fb, 0, 2 * (k * mx.nbp + nb));
+#pragma unroll
+                    for (int j = 0; j < NB2; j++) {  // weight block nb NB2 + j: B rows and its scale record
+                        const int wb = nb * NB2 + j;
+                        tma_load_2d_pair(sB + stage * C::B_BYTES + j * 8192, &tmB, fb, k * 128, wb * 128 + rank * 64);
+                        tma_load_2d_pair(sSF + stage * C::SF_BYTES + j * 512, &tmSF, fb, 0, 2 * (k * mx.nbp + wb));
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1;
@@ -122,7 +135,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
             uint32_t ph = 0;
             bool ok = true;
             for (int t = pair, i = 0; t < total && ok; t += npairs, i++) {
-                const uint32_t buf = i & 1, tph = (i >> 1) & 1;  // group i & 1's buffer, its use count's parity
+                // NB2 = 1: group i & 1's buffer and its use count's parity; NB2 = 2: the one buffer
+                const uint32_t buf = NB2 == 1 ? (i & 1) : 0, tph = NB2 == 1 ? (i >> 1) & 1 : i & 1;
                 for (int k = 0; k < KI; k++) {
                     if (k == 0) {
                         if (!(ok = mbar_wait(&tempty[buf], tph ^ 1, g.err, XTB_ERR_WAIT_TMEM))) break;
@@ -133,12 +147,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                     const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
                     // in issue order after the previous slice's MMAs (the tensor core keeps its order)
-                    tmem_cp_pair_32x128b_x4(sfb, sdesc_rows16(smem_u32(sSF + stage * C::SF_BYTES)));
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        umma_pair_mx(tbase + buf * C::BN, sdesc(a0 + kk * 32, 1024, SWZ_128B),
-                                     sdesc(b0 + kk * 32, 1024, SWZ_128B), idesc_mx_m256(C::BN, kk, kk), sfa, sfb,
-                                     (k > 0 || kk > 0));
+                    for (int j = 0; j < NB2; j++)
+                        tmem_cp_pair_32x128b_x4(sfb + 8 * j, sdesc_rows16(smem_u32(sSF + stage * C::SF_BYTES + j * 512)));
+#pragma unroll
+                    for (int j = 0; j < NB2; j++)
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_pair_mx(tbase + buf * 128 + j * 128, sdesc(a0 + kk * 32, 1024, SWZ_128B),
+                                         sdesc(b0 + j * 8192 + kk * 32, 1024, SWZ_128B), idesc_mx_m256(128, kk, kk), sfa,
+                                         sfb + 8 * j, (k > 0 || kk > 0));
                     umma_commit_pair(&empty[stage], 0x3);
                     if (k == KI - 1) umma_commit_pair(&tfull[buf], 0x3);
                     if (++stage == STAGES) {
@@ -159,17 +177,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         cx.tmC = &tmC;
         uint32_t tph = 0;
         bool ok = true;
-        for (int t = pair + grp * npairs; t < total && ok; t += 2 * npairs) {
+        // NB2 = 1: the groups take the pair's tiles in turn, each in its own buffer; NB2 = 2: both take every tile,
+        // group g its columns 128 g .. 128 g + 127 (in TMEM and in the output), from the one buffer
+        const int bufi = NB2 == 1 ? grp : 0;
+        for (int t = pair + (NB2 == 1 ? grp * npairs : 0); t < total && ok; t += (NB2 == 1 ? 2 : 1) * npairs) {
             const int nb = t % g.n_tiles, mb = t / g.n_tiles;
             cx.row0 = mb * 256 + rank * 128 + quad * 32;
-            cx.col0 = nb * C::BN;
+            cx.col0 = nb * C::BN + (NB2 == 1 ? 0 : grp * 128);
             typename Epi::State es;
             Epi::begin(ep, cx, es);
             const float s = g.ascale * Epi::col_scale(ep, cx);
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[grp], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&tfull[bufi], tph, g.err, XTB_ERR_WAIT_TMEM)))) break;
             tph ^= 1;
             tc_fence_after();
-            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + grp * C::BN;
+            const uint32_t taddr = tbase + ((uint32_t)(quad * 32) << 16) + grp * 128;  // either layout
             if constexpr (StreamOf<Epi>::v) {
                 float v[2][32];
                 tmem_ld16(taddr, v[0]);
@@ -183,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                     } else {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive_cluster(tempty0 + grp * 8);
+                        if (lane == 0) mbar_arrive_cluster(tempty0 + bufi * 8);
                     }
                     Epi::apply_chunk(ep, v[c & 1], s, c, cx, es);
                 }
@@ -202,7 +223,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(tempty0 + grp * 8);
+                if (lane == 0) mbar_arrive_cluster(tempty0 + bufi * 8);
                 Epi::apply(ep, (float *)acc, cx, es);
             }
         }

@@ -149,15 +149,16 @@ int sf_map(CUtensorMap *m, const uint8_t *sf, int n, int k)
     return make_tmap_2d(m, sf, 256, rows, 256, 256, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-// One launch of the CTA-pair block-scaled GEMM (power-of-two block scales, w.sf, w.sfmap): 256 x 128 tiles.
-template <class Epi>
+// One launch of the CTA-pair block-scaled GEMM (power-of-two block scales, w.sf, w.sfmap): 256 x 128 tiles, or
+// 256 x 256 (NB2 = 2: two weight blocks per tile).
+template <class Epi, int NB2>
 static int run_gemm2_mx(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep,
                         cudaStream_t st, const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
 {
-    using Cfg = Gemm2MxCfg<StagingOf<Epi>::v>;
-    auto kern = k_gemm2_mx<Epi>;
+    using Cfg = Gemm2MxCfg<StagingOf<Epi>::v, NB2>;
+    auto kern = k_gemm2_mx<Epi, NB2>;
     if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
-    if (!w.sf || a.row_bytes != w.op.row_bytes || M <= 0 || a.box_rows != A_BOX_ROWS || w.op.box_rows != Cfg::BN / 2) {
+    if (!w.sf || a.row_bytes != w.op.row_bytes || M <= 0 || a.box_rows != A_BOX_ROWS || w.op.box_rows != 64) {
         fprintf(stderr, "eva: pair mx gemm operands (scale image %p, K bytes %d vs %d, boxes %d / %d rows, M %d)\n",
                 (const void *)w.sf, a.row_bytes, w.op.row_bytes, a.box_rows, w.op.box_rows, M);
         return -1;
@@ -237,8 +238,9 @@ static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, con
                     const CUtensorMap *tmc = nullptr, uint32_t *err = nullptr)
 {
     if (w.sf)  // power-of-two block scales
-        return w.sf_pair ? run_gemm2_mx<Epi>(a, w, M, ascale, ep, st, tmc, err)
-                         : run_gemm_mx<Epi>(a, w, M, ascale, ep, st, tmc, err);
+        return !w.sf_pair ? run_gemm_mx<Epi>(a, w, M, ascale, ep, st, tmc, err)
+               : w.sf_wide ? run_gemm2_mx<Epi, 2>(a, w, M, ascale, ep, st, tmc, err)
+                           : run_gemm2_mx<Epi, 1>(a, w, M, ascale, ep, st, tmc, err);
     if (!kPairG[U] && w.uniform > 0.0f) {  // one scale for the whole weight: accumulate over K in TMEM, scale once
         if constexpr (kPair[U])
             return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
@@ -566,6 +568,12 @@ int prepare_kernels()
                               Gemm2MxCfg<StagingOf<EpiFC2>::v>::SMEM, Gemm2MxCfg<StagingOf<EpiResid>::v>::SMEM};
         for (int i = 0; i < 4; i++)
             if (set_smem(k2[i], sm2[i]) || max_pairs(k2[i], 320, sm2[i]) <= 0) return -1;
+        const void *k2w[] = {(const void *)k_gemm2_mx<EpiQKV, 2>, (const void *)k_gemm2_mx<EpiFC2, 2>,
+                             (const void *)k_gemm2_mx<EpiResid, 2>};
+        const size_t sm2w[] = {Gemm2MxCfg<StagingOf<EpiQKV>::v, 2>::SMEM, Gemm2MxCfg<StagingOf<EpiFC2>::v, 2>::SMEM,
+                               Gemm2MxCfg<StagingOf<EpiResid>::v, 2>::SMEM};
+        for (int i = 0; i < 3; i++)
+            if (set_smem(k2w[i], sm2w[i]) || max_pairs(k2w[i], 320, sm2w[i]) <= 0) return -1;
     }
     return 0;
 }

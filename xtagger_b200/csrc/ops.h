@@ -45,6 +45,8 @@ struct Weight8 {
     int sf_nbp = 0;
     // run on the CTA-pair block-scaled kernel (gemm2_mx.cuh: the operand op in 64-row boxes, sfmap over sf)
     bool sf_pair = false;
+    // on the pair kernel, 256-column tiles (two weight blocks per tile, one accumulator): half the A traffic per FLOP
+    bool sf_wide = false;
     CUtensorMap sfmap;
 };
 // The scale-factor image as the pair kernel's tensor map (512-byte records as 2 rows of 256 bytes).
