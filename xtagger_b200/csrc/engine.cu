@@ -397,10 +397,10 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
         // blocks per tile, half the A traffic per FLOP) for those in kMxWide (N a multiple of 256), else 256 x 128.
         // Measured in the batch-64 forward (power-capped clocks, ms per forward): fc2 4.97 on the pair's wide tiles
         // against 6.2 on the promoting pair and 6.5 on 128-column block-scaled tiles; QKV 4.41 wide against 4.95 on
-        // 128-column tiles and 5.3 on one CTA; the out-projection 1.86 on 128-column tiles against 1.96 wide and 2.4
-        // promoting; fc1 8.1 on one CTA against 8.25 on the pair.
+        // 128-column tiles and 5.3 on one CTA; fc1 7.25-7.6 wide against 8.3 on one CTA and 8.25 on 128-column pair
+        // tiles; the out-projection 1.86 on 128-column tiles against 1.96 wide and 2.4 promoting.
         // XTB_MX_KINDS / XTB_MX_PAIR / XTB_MX_WIDE (hex masks) in the environment override these for measurements.
-        int kMxKinds = 0xF, kMxPair = 0xB, kMxWide = 0x9;
+        int kMxKinds = 0xF, kMxPair = 0xF, kMxWide = 0xD;
         if (const char *m = getenv("XTB_MX_KINDS")) kMxKinds = (int)strtol(m, nullptr, 16);
         if (const char *m = getenv("XTB_MX_PAIR")) kMxPair = (int)strtol(m, nullptr, 16);
         if (const char *m = getenv("XTB_MX_WIDE")) kMxWide = (int)strtol(m, nullptr, 16);
@@ -436,7 +436,8 @@ int replica_up(Impl *im, Replica &r, eva *e, const uint8_t *hostblob)
                         w.sf = r.sfimg + off[g] + (size_t)i * per[g];
                         w.sf_nbp = ((w.n + 127) / 128 + 1) & ~1;
                         w.sf_pair = (kMxPair >> g) & 1;
-                        w.sf_wide = w.sf_pair && ((kMxWide >> g) & 1) && w.n % 256 == 0;
+                        // wide tiles need N a multiple of 256, or an epilogue that skips a half tile past N (fc1's)
+                        w.sf_wide = w.sf_pair && ((kMxWide >> g) & 1) && (w.n % 256 == 0 || g == W_FC1);
                         // the block-scaled kernels' B boxes: 256 rows (one CTA) or 64 per CTA (pair)
                         RCK(make_operand(&w.op, w.op.ptr, w.n, w.k, w.sf_pair ? 64 : 256));
                         if (w.sf_pair) RCK(sf_map(&w.sfmap, w.sf, w.n, w.k));

@@ -569,10 +569,10 @@ int prepare_kernels()
         for (int i = 0; i < 4; i++)
             if (set_smem(k2[i], sm2[i]) || max_pairs(k2[i], 320, sm2[i]) <= 0) return -1;
         const void *k2w[] = {(const void *)k_gemm2_mx<EpiQKV, 2>, (const void *)k_gemm2_mx<EpiFC2, 2>,
-                             (const void *)k_gemm2_mx<EpiResid, 2>};
+                             (const void *)k_gemm2_mx<EpiResid, 2>, (const void *)k_gemm2_mx<EpiFC1, 2>};
         const size_t sm2w[] = {Gemm2MxCfg<StagingOf<EpiQKV>::v, 2>::SMEM, Gemm2MxCfg<StagingOf<EpiFC2>::v, 2>::SMEM,
-                               Gemm2MxCfg<StagingOf<EpiResid>::v, 2>::SMEM};
-        for (int i = 0; i < 3; i++)
+                               Gemm2MxCfg<StagingOf<EpiResid>::v, 2>::SMEM, Gemm2MxCfg<StagingOf<EpiFC1>::v, 2>::SMEM};
+        for (int i = 0; i < 4; i++)
             if (set_smem(k2w[i], sm2w[i]) || max_pairs(k2w[i], 320, sm2w[i]) <= 0) return -1;
     }
     return 0;
