@@ -104,8 +104,8 @@ int eva_launches_per_forward(eva *e);
  * otherwise 0 (the dense kernels are faster on the same weights). */
 int eva_sparse_kinds(eva *e);
 /* Projection kinds (bit 0 QKV, 1 O, 2 W12, 3 W2) running on the tensor core's own block scaling: block-scaled (v4)
- * weights whose block scales are all powers of two, in every layer: QKV, O and W12, where it measures faster
- * (XTB_MX=0 in the environment at open keeps the promoting kernels). */
+ * weights whose block scales are all powers of two, in every layer: all four by default (XTB_MX=0 in the
+ * environment at open keeps the promoting kernels; XTB_MX_KINDS, a hex mask, chooses the kinds). */
 int eva_block_scale_kinds(eva *e);
 /* One direct (non-graph) forward on device 0 with an event after every kernel; per-kernel-kind milliseconds into
  * ms[kinds] (names from eva_prof_name), returns the number of kinds or -1. Mirrors the reference's EVA_PROF
