@@ -47,3 +47,43 @@ def test_prof_names(xlib):
     names = [xlib.eva_prof_name(i) for i in range(9)]
     assert all(names) and xlib.eva_prof_name(9) is None
     assert names[2] == b"qkv" and names[3] == b"attention"
+
+
+def test_scale_factor_image_layout(xlib):
+    """xtb_sf_image (host code): records [k block][n block, count padded to even][512 bytes], every byte of a record
+    the UE8M0 exponent of that block's power-of-two scale; the padding block's record is 2^0, so a 256-column tile of
+    the CTA-pair kernel always has a record for its second weight block. Scales that are not positive normal powers
+    of two are refused and leave the image untouched."""
+    import numpy as np
+    n, k = 5472, 1024                                     # 43 weight blocks (padded to 44) x 8 K blocks
+    nbn, nbk, nbp = 43, 8, 44
+    assert xlib.xtb_sf_image_bytes(n, k) == nbk * nbp * 512
+    rng = np.random.default_rng(5)
+    e = rng.integers(100, 140, size=(nbn, nbk))
+    ws = np.ldexp(1.0, e - 127).astype(np.float32)
+    img = np.zeros(nbk * nbp * 512, np.uint8)
+    assert xlib.xtb_sf_image(ws.ctypes.data, n, k, img.ctypes.data) == 0
+    rec = img.reshape(nbk, nbp, 512)
+    assert np.all(rec == rec[:, :, :1])                   # uniform records
+    np.testing.assert_array_equal(rec[:, :nbn, 0], e.T)
+    assert np.all(rec[:, nbn, 0] == 127)
+    for bad in (3.0, 0.0, -0.5, np.inf, 2.0 ** -130):     # not a power of two / zero / negative / inf / subnormal
+        w2 = ws.copy()
+        w2[7, 3] = bad
+        img2 = np.full_like(img, 0xAB)
+        assert xlib.xtb_sf_image(w2.ctypes.data, n, k, img2.ctypes.data) == -1
+        assert np.all(img2 == 0xAB)
+
+
+def test_block_scaled_gemm_argument_checks(xlib):
+    """xtb_gemm_mx_f32 refuses bad arguments on the host, before any device work: no scale image, K not a multiple
+    of 16, an unknown kernel form (pair outside 0..2), no rows, an output stride below N."""
+    import numpy as np
+    buf = np.zeros(1 << 16, np.uint8)
+    p = buf.ctypes.data
+    assert xlib.xtb_gemm_mx_f32(p, 16, 64, p, 256, None, 1, 1.0, p, 256, None) == -1
+    assert xlib.xtb_gemm_mx_f32(p, 16, 60, p, 256, p, 1, 1.0, p, 256, None) == -1
+    assert xlib.xtb_gemm_mx_f32(p, 16, 64, p, 256, p, 3, 1.0, p, 256, None) == -1
+    assert xlib.xtb_gemm_mx_f32(p, 16, 64, p, 256, p, -1, 1.0, p, 256, None) == -1
+    assert xlib.xtb_gemm_mx_f32(p, 0, 64, p, 256, p, 1, 1.0, p, 256, None) == -1
+    assert xlib.xtb_gemm_mx_f32(p, 16, 64, p, 256, p, 1, 1.0, p, 128, None) == -1
