@@ -17,7 +17,9 @@
 // NB2 = 2 (wide tiles): a pair computes 256 x 256 tiles as two M = 256, N = 128 MMAs per 128-byte K slice, one per
 // 128-row weight block, each with that block's own uniform scale record (B scale factors at columns 288 and 296), so
 // each A slice brought into shared memory serves 256 output columns instead of 128: half the A traffic per FLOP,
-// for projections whose A operand streams from DRAM (fc2: K = 2736). The tile's accumulator fills columns 0 .. 255,
+// which bounds fc2 (K = 2736, A streamed from DRAM) and speeds up QKV and fc1 as well; N need not be a multiple
+// of 256 when the epilogue skips a half tile past N (the B rows there read as the TMA fill value, and the scale
+// image's block count is even, so the second record exists). The tile's accumulator fills columns 0 .. 255,
 // so there is one buffer: epilogue group g drains columns 128 g .. 128 g + 127 of every tile, and the next tile's
 // MMAs start once both groups of both CTAs have read it.
 #pragma once
