@@ -83,10 +83,11 @@ def cpu_sample(model, nimg=1):
     from oracle import oracle as O
     from xtagger_b200 import model as M
     x = M.synthetic_inputs(nimg, seed=1)
+    cores = O.use_all_cores()   # not OMP_NUM_THREADS, which torch.distributed.run sets to 1
     t0 = time.perf_counter()
     O.forward(model, x)   # the reference's attention tiling (64-key tiles, 16-row slices)
     dt = time.perf_counter() - t0
-    return nimg / dt, O.lib().or_threads(), dt
+    return nimg / dt, cores, dt
 
 
 def run_reference(args, rank, world):

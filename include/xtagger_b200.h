@@ -113,7 +113,9 @@ int eva_block_scale_kinds(eva *e);
 int eva_profile(eva *e, float *ms, int kinds);
 const char *eva_prof_name(int kind);
 
-/* ---- kernel-level entry points (device pointers, enqueued on `stream`, no allocation) ---- */
+/* ---- kernel-level entry points (device pointers, enqueued on `stream`) ----
+ * None of them allocates device memory; the first call on a device looks up the library's static error word and
+ * sets the kernels' shared-memory attributes, so it should come before any stream capture. */
 /* D[m][n] fp32 = ascale * sum_kb wscale[n/128][kb] * sum_{k in kb} e4m3(A[m][k]) * e4m3(W[n][k]).
  * A: E4M3 [m][k], W: E4M3 [n][k], wscale: fp32 [ceil(n/128)][ceil(k/128)], k a multiple of 16. */
 int xtb_gemm_e4m3_f32(const uint8_t *a, int m, int k, const uint8_t *w, int n, const float *wscale, float ascale,
@@ -153,13 +155,13 @@ int xtb_head_f16(const uint16_t *hw, int nt, const uint16_t *pn, int nimg, const
 int xtb_head_e4m3(const uint8_t *hw8, int nt, const float *hws, const uint8_t *pn8, int nimg, float ascale,
                   const float *hb, float *out, void *stream);
 
-/* fc2 as xtb_fc2, allocating nothing: its scratch (per-row mean / rstd, bounded-wait status) lives in a static
- * device array of the library, sized for XTB_NOALLOC_MAX_ROWS rows. No counterpart in the reference. For callers
- * that cannot let the library allocate device memory (their own fixed memory arena, no cudaMalloc
- * synchronisation on a latency-critical path, no out-of-memory failure after start-up). `stat` (fc1's partials)
- * is only read. Rows beyond the maximum are rejected (-1). The first call on a device sets up the array's address
- * and should come before any stream capture. All calls on a device share the array: calls that overlap on the GPU
- * race and must be serialised by the caller. */
+/* fc2 as xtb_fc2, allocating nothing: its scratch (per-row mean / rstd) lives in a static device array of the
+ * library, sized for XTB_NOALLOC_MAX_ROWS rows. No counterpart in the reference. For callers that cannot let the
+ * library allocate device memory (their own fixed memory arena, no cudaMalloc synchronisation on a latency-critical
+ * path, no out-of-memory failure after start-up). `stat` (fc1's partials) is only read. Rows beyond the maximum are
+ * rejected (-1). A bounded wait that runs out sets a bit of the device's error word (xtb_error_word). The first call
+ * on a device sets up the array's address and should come before any stream capture. All calls on a device share
+ * the array: calls that overlap on the GPU race and must be serialised by the caller. */
 #define XTB_NOALLOC_MAX_ROWS (16 * 1025)
 int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x,
                     const float *stat, const float *c, const float *d, void *stream);
@@ -168,6 +170,12 @@ int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, const float *
  * |x[row][c]|) for an fp16 [rows][k] tensor (k a multiple of 8, 16-byte aligned); amax holds non-negative fp32 values
  * (start from zeros). Used by the calibration forward (xtagger_b200/calib.py). */
 int xtb_amax_f16(const uint16_t *x, int k, int rows, float *amax, void *stream);
+
+/* The E4M3 encoder of every epilogue, over an array: y[i] = E4M3(x[i]) (round to nearest even, finite values beyond
+ * 448 saturate, NaN stays NaN), pairs packed as __nv_cvt_float2_to_fp8x2(..., __NV_SATFINITE, __NV_E4M3), the
+ * reference's q2 (kern_common.cuh:96-100); with via_f16 the attention output's staging: y[i] = E4M3(fp16(x[i]))
+ * (kern_common.cuh:527-541). x fp32, y bytes, device pointers. For the encoder's exhaustive parity tests. */
+int xtb_e4m3_encode(const float *x, uint8_t *y, size_t n, int via_f16, void *stream);
 
 /* ---- 2:4-sparse weights on the sparse tensor cores (tcgen05.mma.sp) ----
  * The reference prunes weights 2:4 offline (prune24.py:44-56: in every group of four consecutive k the two least
@@ -229,8 +237,9 @@ int xtb_prep_kernels(int w, int h, int x0, int y0, int cw, int ch);
  * with no CUDA binding of their own (e.g. scores of eva_output back to the host after a device-side batch). */
 int xtb_copy_async(void *dst, const void *src, size_t bytes, void *stream);
 
-/* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). The engine copies it
- * back with every batch; eva_wait returns NULL (with an "eva:" line) for a batch after which it is set. */
+/* Library error word of a device: bits set by kernels whose bounded waits ran out (0 = healthy). A static device
+ * array of the library (no allocation). The engine copies it back with every batch; eva_wait returns NULL (with an
+ * "eva:" line) for a batch after which it is set. Reading and clearing synchronise with the device. */
 uint32_t xtb_error_word(int device);
 void xtb_error_clear(int device);
 /* Failure-path self-test on the current device: a kernel waits at most timeout_us (<= 10 s) on a barrier that is

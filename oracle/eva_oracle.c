@@ -19,6 +19,13 @@
 #define EPS 1e-6f    /* kern_common.cuh:16 */
 
 int or_threads(void) { return omp_get_max_threads(); }
+/* threads of the oracle's parallel regions from now on (whatever OMP_NUM_THREADS said; torch.distributed.run sets
+ * it to 1); returns the new count */
+int or_set_threads(int n)
+{
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+}
 
 /* ---------------------------------------------------------------------------------------------------------------
  * E4M3 (OCP FP8, 1-4-3, bias 7, no infinities, 0x7F / 0xFF NaN, max finite 448). The reference converts with

@@ -66,6 +66,7 @@ int or_model_nt(const char *model);
 void or_prune24(uint8_t *w, int n, int k, int wanda);
 
 int or_threads(void);
+int or_set_threads(int n);                    /* threads of later parallel regions (OMP_NUM_THREADS overridden) */
 
 /* PixAI tagger (px_oracle.c; src/engine/px.h + px_kernels.cu): window-major tokens, sequences of L tokens */
 void or_px_embed(const uint16_t *in, int rows, const uint16_t *pe, const float *pos, const float *w, const float *b,

@@ -53,6 +53,7 @@ def lib():
             "or_model_nt": (C.c_int, [C.c_char_p]),
             "or_prune24": (None, [_u8, C.c_int, C.c_int, C.c_int]),
             "or_threads": (C.c_int, []),
+            "or_set_threads": (C.c_int, [C.c_int]),
             "or_div255": (C.c_uint32, [C.c_uint32]),
             "or_over_white": (None, [_u8, C.c_int, C.c_int, C.c_int, C.c_int]),
             "or_half": (None, [_u8, C.c_int, C.c_int, C.c_int, _u8, C.c_int]),
@@ -76,6 +77,12 @@ def lib():
             f.argtypes = args
         _lib = l
     return _lib
+
+
+def use_all_cores():
+    """Run the oracle's parallel regions on every core this process may use (torch.distributed.run sets
+    OMP_NUM_THREADS=1 for its workers); returns the thread count."""
+    return lib().or_set_threads(len(os.sched_getaffinity(0)))
 
 
 def e4m3(x):

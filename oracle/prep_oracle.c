@@ -3,13 +3,13 @@
  * apart) -> alpha over white -> 2x2 box pyramid -> a crop rect resampled into a 448 x 448 white square with the
  * antialiased bicubic -> fp16 in [-1, 1], BGR planes, patch-operand layout (eva.h:15-16).
  *
- * Parity: procimg.h includes the Windows-only engine headers and cannot be built here, so this restatement is pinned
- * by the tests' exact known answers (the /255 rounding over its whole domain, the box rounding rules, the identity
- * path for every byte value) and the GPU kernels are checked against it bit for bit. Float arithmetic follows the
+ * Parity: procimg.h includes the Windows-only engine headers and cannot be built whole here; its preprocessing
+ * functions are cut out of it and compiled with the reference's release flags by tests/golden/make_prep_golden.py,
+ * and this restatement is bit-identical to them on every case of tests/golden/golden_prep.json (besides the tests'
+ * exact known answers); the GPU kernels are checked against it bit for bit. Float arithmetic follows the
  * reference's source order with one rounding per operation (this file is compiled with -ffp-contract=off), and
- * fmaf where the reference uses fused multiply-adds (_mm256_fmadd_ps in pi_vrow, _mm_fmadd_ps in pi_hrow and
- * pi_idrow). A build of the reference whose compiler contracted pi_cubic / pi_axis into FMAs could differ from
- * this in the last bit of a filter weight. */
+ * fmaf where the reference computes a fused multiply-add: its intrinsics (_mm256_fmadd_ps in pi_vrow, _mm_fmadd_ps in
+ * pi_hrow and pi_idrow) and the products its compiler contracts (pi_cubic, the white-tap constant of pi_axis). */
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -89,11 +89,14 @@ static void pyr_build(or_pyr *p, const uint8_t *img, int w, int h, int stride)
     }
 }
 
-/* Keys bicubic, a = -0.5 (pi_cubic, procimg.h:751-756) */
+/* Keys bicubic, a = -0.5 (pi_cubic, procimg.h:751-756), as the reference's release build computes it: GCC at -O3 with
+ * FMA available (src/CMakeLists.txt:38,73) contracts each multiply whose product feeds one add into a fused
+ * multiply-add, so (1.5 x - 2.5) x x + 1 is fma(fma(1.5, x, -2.5) x, x, 1) and the second branch a chain of three. */
 static float cubic(float x)
 {
     x = x < 0 ? -x : x;
-    return x < 1.0f ? (1.5f * x - 2.5f) * x * x + 1.0f : x < 2.0f ? ((-0.5f * x + 2.5f) * x - 4.0f) * x + 2.0f : 0.0f;
+    return x < 1.0f ? fmaf(fmaf(1.5f, x, -2.5f) * x, x, 1.0f)
+         : x < 2.0f ? fmaf(fmaf(fmaf(-0.5f, x, 2.5f), x, -4.0f), x, 2.0f) : 0.0f;
 }
 
 /* One axis of the resample (pi_axis, procimg.h:761-795): virtual white square [0, side) -> [0, S), content at
@@ -128,7 +131,7 @@ static void axis(int S, int side, int off, int len, int mt, float sc, float add,
         for (int j = 0; j < b - a; j++) wi[j] *= sum;
         s[i] = a - off;
         n[i] = b - a;
-        k[i] = 255.0f * white * sum + add;
+        k[i] = fmaf(255.0f * white, sum, add);   /* contracted in the reference's build, as cubic */
     }
 }
 

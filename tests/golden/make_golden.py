@@ -1,6 +1,6 @@
 """Generate the golden vectors that pin the CPU oracle to the reference's own code.
 
-Run in a container where the reference tree is available (its path in $XTAGGER_REF, default /root/reference);
+Run in a container where the reference tree is available (its path in $XTAGGER_REF, default: a checkout named "reference" beside this repository);
 the outputs are small committed fixtures in this directory, so the tests never need the reference at run time.
 
   golden_e4m3.npz      inputs and E4M3 codes of the reference's weight quantiser (src/tools/export_eva.py:64-66,
@@ -23,7 +23,8 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("XTAGGER_REF", "/root/reference")
+REPO = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("XTAGGER_REF", os.path.join(os.path.dirname(REPO), "reference"))
 
 D, T, NP, K0P, HIDP, NL = 1024, 1025, 1024, 592, 2736, 24
 

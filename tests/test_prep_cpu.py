@@ -1,8 +1,11 @@
 """The preprocessing oracle (oracle/prep_oracle.c, a restatement of src/core/procimg.h's wd path) pinned by exact
 known answers on the CPU: the /255 rounding over its whole domain, alpha over white, the box pyramid's rounding
 rules, the scale-1 path for every byte value, the level choice, and the bicubic resample against an independent
-float64 implementation of the same filter. procimg.h itself needs the Windows-only engine headers and cannot be
-built here."""
+float64 implementation of the same filter; and bit for bit against the reference's own preprocessing functions, cut
+out of procimg.h and compiled by tests/golden/make_prep_golden.py (procimg.h as a whole needs the Windows-only engine
+headers and cannot be built here)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -145,3 +148,26 @@ def test_prep_kernel_counts(xlib, args, n):
     """Kernels per call: ingest = alpha pass + one per pyramid level above 0; crop = 1 on the normalise-only path,
     3 (tables, vertical, horizontal) when resampling; bad rects -1. Host arithmetic only, no device."""
     assert xlib.xtb_prep_kernels(*args) == n
+
+
+def test_oracle_matches_the_reference_preprocessing():
+    """The oracle against the reference's own preprocessing: procimg.h's pi_row_rgbx / pi_pyramid / pi_prep (and the
+    functions they call), extracted from the reference at generation time and compiled with its release flags
+    (tests/golden/make_prep_golden.py), on seeded images through the identity path, resamples up and down from level
+    0 and from pyramid levels 1 and 2, odd sizes and rects, with and without alpha: every output bit-identical (sha256
+    of each model input in tests/golden/golden_prep.json)."""
+    import hashlib
+    import json
+
+    from oracle import oracle as O
+    from tests.golden.prep_case import cases, image
+    want = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_prep.json")))
+    bad = []
+    for name, w, h, alpha, seed, rects in cases():
+        for i, (x0, y0, cw, ch) in enumerate(rects):
+            img = image(w, h, alpha, seed)
+            out = np.zeros((1024, 592), np.uint16)
+            O.lib().or_prep(img.reshape(-1), w, h, 4 * w, alpha, x0, y0, cw, ch, out.reshape(-1))
+            if hashlib.sha256(out.tobytes()).hexdigest() != want[name][i]:
+                bad.append((name, i))
+    assert not bad, f"oracle outputs that differ from the reference's preprocessing: {bad}"

@@ -1,8 +1,13 @@
 """GPU preprocessing (xtb_prep_ingest / xtb_prep_crop) against the CPU oracle's restatement of procimg.h's wd path,
 bit for bit: every output half, and the image modified in place by alpha over white. Cases cover the scale-1 path
 (whole 448-pixel sides, a 448 crop, vertical white pad), upscaling with white borders, downscaling from level 0 and
-from pyramid levels 1 and 2, crops, an extreme aspect ratio and padded row strides."""
+from pyramid levels 1 and 2, crops, an extreme aspect ratio and padded row strides. Then directly against the
+reference's own preprocessing functions (procimg.h compiled with the reference's flags by
+tests/golden/make_prep_golden.py): the sha256 of every output of tests/golden/golden_prep.json."""
 import ctypes as C
+import hashlib
+import json
+import os
 
 import numpy as np
 import pytest
@@ -121,3 +126,21 @@ def test_prep_feeds_engine_in_place(xlib, cuda, tmp_path):
     assert np.isfinite(got).all()
     assert np.array_equal(got, want)
     assert L.EVA_IN == 1024 * 592
+
+
+def test_prep_matches_the_reference_preprocessing(xlib, cuda):
+    import torch
+    from tests.golden.prep_case import cases, image
+    want = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_prep.json")))
+    bad = []
+    for name, w, h, alpha, seed, rects in cases():
+        for i, (x0, y0, cw, ch) in enumerate(rects):
+            dimg = G.dev(image(w, h, alpha, seed))
+            scratch = G.zeros((xlib.xtb_prep_scratch_bytes(w, h),), torch.uint8)
+            out = G.zeros((1024 * 592,), torch.int16)
+            assert xlib.xtb_prep_ingest(G.P(dimg), w, h, 4 * w, alpha, G.P(scratch), None) == 0
+            assert xlib.xtb_prep_crop(G.P(dimg), w, h, 4 * w, x0, y0, cw, ch, G.P(scratch), G.P(out), None) == 0
+            if hashlib.sha256(G.host(out).tobytes()).hexdigest() != want[name][i]:
+                bad.append((name, i))
+            G.release()
+    assert not bad, f"GPU outputs that differ from the reference's preprocessing: {bad}"

@@ -1,6 +1,20 @@
-"""xtb_fc2_noalloc -- fc2 with its scratch in a static device array, for callers that cannot let the library
-allocate device memory -- against xtb_fc2 through the C ABI, on two calls in a row (the second with fewer rows,
-so a stale tail of the shared array from the first call would show)."""
+"""xtb_fc2_noalloc through the C ABI.
+
+It is fc2 for callers that cannot let the library allocate device memory and cannot lend it scratch either: an
+application that hands out every byte of GPU memory from its own arena, or one on a latency-critical path that cannot
+afford cudaMalloc's implicit device-wide synchronisation. xtb_fc2 writes each row's (mean, rstd) over the caller's fc1
+partials; xtb_fc2_noalloc leaves them untouched and keeps that scratch in a static device array of the library.
+
+Checked on two calls in a row (the second with fewer rows, so a stale tail of the shared array from the first call
+would show): bit-identical to xtb_fc2 (the same GEMM launch, and row statistics summed in the same order), within the
+fc2 tolerance of the oracle, the library's error word still 0 (a bounded wait that runs out inside the call would
+set it), the caller's partials unchanged. In a fresh process whose CUDA modules are loaded eagerly (so that loading
+the library's code cannot be mistaken for an allocation), free device memory is the same before the first call and
+after two calls. Collected last, so that a run stopping at the first failure has run every other test."""
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -8,6 +22,7 @@ from tests import _gpu as G
 
 pytestmark = pytest.mark.gpu
 
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 D, HIDP, HID, NSTAT = 1024, 2736, 2730, 43
 
 
@@ -30,11 +45,14 @@ def _case(rng, rows):
     return h8, w, ws, stat, c, d, x0
 
 
-def test_noalloc_matches_fc2_on_two_calls(xlib, cuda):
+def test_noalloc_matches_fc2_and_oracle_on_two_calls(xlib, cuda):
+    from oracle import oracle as O
+    xlib.xtb_error_clear(0)
     rng = np.random.default_rng(31)
+    adq = 3 / 448
     for rows in (2 * 1025, 1025 + 77):
         h8, w, ws, stat, c, d, x0 = _case(rng, rows)
-        args = lambda x, st: (G.P(G.dev(h8)), rows, G.P(G.dev(w)), G.P(G.dev(ws)), 3 / 448, G.P(x), G.P(st),
+        args = lambda x, st: (G.P(G.dev(h8)), rows, G.P(G.dev(w)), G.P(G.dev(ws)), adq, G.P(x), G.P(st),  # noqa
                               G.P(G.dev(c)), G.P(G.dev(d)), None)
         x_ref, st_ref = G.dev(x0), G.dev(stat)
         assert xlib.xtb_fc2(*args(x_ref, st_ref)) == 0
@@ -42,7 +60,12 @@ def test_noalloc_matches_fc2_on_two_calls(xlib, cuda):
         assert xlib.xtb_fc2_noalloc(*args(x_na, st_na)) == 0
         G.check_error_word(xlib)
         got, want = G.host(x_na).view(np.uint16), G.host(x_ref).view(np.uint16)
-        G.assert_f16_close(got, want, 1e-2, f"noalloc fc2 ({rows} rows)")
+        assert np.array_equal(got, want), f"{rows} rows: {int((got != want).sum())} outputs differ from xtb_fc2"
+        oracle = x0.copy()
+        s = stat[:, :, 0].astype(np.float64).sum(0)
+        q = stat[:, :, 1].astype(np.float64).sum(0)
+        O.lib().or_fc2_epilogue(oracle, O.gemm_e4m3(h8, w, ws, adq), rows, s, q, c, d)
+        G.assert_f16_close(got, oracle, 1e-2, f"noalloc fc2 vs oracle ({rows} rows)")
         assert np.array_equal(G.host(st_na), stat)          # the caller's partials are only read
         G.release()
 
@@ -53,3 +76,39 @@ def test_noalloc_rejects_rows_beyond_the_static_scratch(xlib, cuda):
     x = G.zeros((8, D), torch.int16)
     assert xlib.xtb_fc2_noalloc(G.P(x), rows, G.P(x), G.P(x), 1.0, G.P(x), G.P(x), G.P(x), G.P(x), None) == -1
     assert xlib.xtb_fc2_noalloc(G.P(x), 0, G.P(x), G.P(x), 1.0, G.P(x), G.P(x), G.P(x), G.P(x), None) == -1
+
+
+_FRESH = r"""
+import ctypes as C, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from xtagger_b200 import lib as L
+xl = L.lib()                                   # the library's code is registered before the context exists
+import torch
+rows = 2050
+dev = torch.device("cuda", 0)
+h8 = torch.zeros((rows, 2736), dtype=torch.uint8, device=dev)
+w = torch.zeros((1024, 2736), dtype=torch.uint8, device=dev)
+ws = torch.ones((8, 22), dtype=torch.float32, device=dev)
+x = torch.zeros((rows, 1024), dtype=torch.float16, device=dev)
+st = torch.ones((43, rows, 2), dtype=torch.float32, device=dev)
+c = torch.zeros(1024, dtype=torch.float32, device=dev)
+d = torch.zeros(1024, dtype=torch.float32, device=dev)
+P = lambda t: C.c_void_p(t.data_ptr())
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info(0)[0]
+for _ in range(2):
+    assert xl.xtb_fc2_noalloc(P(h8), rows, P(w), P(ws), 1.0, P(x), P(st), P(c), P(d), None) == 0
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info(0)[0]
+assert xl.xtb_error_word(0) == 0
+print(free0, free1)
+"""
+
+
+def test_noalloc_first_call_allocates_nothing(cuda):
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
+    r = subprocess.run([sys.executable, "-c", _FRESH, ROOT], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    free0, free1 = map(int, r.stdout.split()[-2:])
+    assert free0 == free1, f"free device memory changed across the first calls: {free0} -> {free1}"

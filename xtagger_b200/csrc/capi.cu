@@ -202,6 +202,16 @@ int xtb_amax_f16(const uint16_t *x, int k, int rows, float *amax, void *stream)
     return launch_amax_f16((const __half *)x, k, rows, amax, S(stream));
 }
 
+int xtb_e4m3_encode(const float *x, uint8_t *y, size_t n, int via_f16, void *stream)
+{
+    if (n && (!x || !y)) return -1;
+    if (n > ((size_t)1 << 40)) {
+        fprintf(stderr, "eva: xtb_e4m3_encode: %zu elements is too many\n", n);
+        return -1;
+    }
+    return launch_e4m3_encode(x, y, n, via_f16, S(stream));
+}
+
 // ---- 2:4-sparse weights ----
 int xtb_sparse24_check(const uint8_t *w, int n, int k) { return sparse24_check(w, n, k); }
 

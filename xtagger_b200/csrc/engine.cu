@@ -664,10 +664,17 @@ int open_common(eva *e, const char *weights, const std::vector<int> &devs, uint3
     }
     for (int s = 0; s < EVA_NBUF; s++) {
         e->hout[s] = (float *)aligned_alloc(4096, (((size_t)nb * e->nt * 4) + 4095) & ~(size_t)4095);
-        if (!e->hout[s]) return -1;
-        if (extra) {
+        if (extra && e->hout[s])
             e->hpn[s] = (uint16_t *)aligned_alloc(4096, (((size_t)nb * D * 2) + 4095) & ~(size_t)4095);
-            if (!e->hpn[s]) return -1;
+        if (!e->hout[s] || (extra && !e->hpn[s])) {
+            fprintf(stderr, "eva: out of host memory for the score slots\n");
+            for (int t = 0; t <= s; t++) {
+                free(e->hout[t]);
+                free(e->hpn[t]);
+            }
+            delete im;
+            memset(e, 0, sizeof(*e));
+            return -1;
         }
     }
     im->bstatus = -1;

@@ -83,6 +83,11 @@ int max_pairs(const void *kern, int threads, size_t smem)
     return n;
 }
 
+// The error words live in a static device array (zero when the library's code is loaded on a device), so that no
+// entry point allocates device memory for them. In host code the name is only a stand-in for the device object:
+// kernels get the address cudaGetSymbolAddress returns for the device, looked up once per device.
+static __device__ __align__(256) uint32_t g_error_words[64];
+
 uint32_t *error_word(int device)
 {
     static uint32_t *words[64];
@@ -91,14 +96,12 @@ uint32_t *error_word(int device)
     if (device < 0 || device >= 64) return nullptr;
     if (!words[device]) {
         int prev = 0;
-        cudaGetDevice(&prev);
-        cudaSetDevice(device);
+        if (cudaGetDevice(&prev) != cudaSuccess) return nullptr;
         void *p = nullptr;
-        if (cudaMalloc(&p, 256) == cudaSuccess) {
-            cudaMemset(p, 0, 256);
-            cudaDeviceSynchronize();
+        if (cudaSetDevice(device) == cudaSuccess && cudaGetSymbolAddress(&p, g_error_words) == cudaSuccess)
             words[device] = (uint32_t *)p;
-        }
+        else
+            fprintf(stderr, "eva: cannot look up the error word on device %d\n", device);
         cudaSetDevice(prev);
     }
     return words[device];

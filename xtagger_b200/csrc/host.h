@@ -31,7 +31,9 @@ int num_sms(int device);
 // device (cudaOccupancyMaxActiveClusters), cached per (kernel, device); 0 on failure.
 int max_pairs(const void *kern, int threads, size_t smem);
 
-// Library error word on the given device (set by kernels whose bounded waits ran out).
+// Library error word on the given device (set by kernels whose bounded waits ran out): a static device array, not an
+// allocation; its address is looked up on the first call for a device (not a stream operation, but keep that first
+// call outside a stream capture, as the engine's bring-up and prepare_kernels() do).
 uint32_t *error_word(int device);
 
 }  // namespace xtb

@@ -3,16 +3,19 @@
 // Some callers cannot let a library allocate device memory: a host application that hands out all GPU memory
 // from its own fixed arena and accounts for every byte, a caller on a latency-critical path that cannot afford
 // cudaMalloc's implicit device-wide synchronisation, or one that must not fail on an out-of-memory at run time
-// after start-up. xtb_fc2 needs two pieces of device scratch beyond its inputs and outputs -- the per-row
-// (mean, rstd) of the SwiGLU output and the word in which kernels record a bounded wait that ran out -- and the
-// library allocates the latter with cudaMalloc on first use. xtb_fc2_noalloc keeps both in one file-scope static
-// device array of fixed size instead, and leaves the caller's fc1 partials untouched.
+// after start-up. xtb_fc2 needs device scratch beyond its inputs and outputs -- the per-row (mean, rstd) of the
+// SwiGLU output, which it writes over the caller's fc1 partials. xtb_fc2_noalloc keeps that scratch in a
+// file-scope static device array of fixed size instead, and leaves the caller's fc1 partials untouched.
+//
+// Failures: a bounded wait inside the GEMM that runs out sets a bit of the library's error word of the device,
+// read with xtb_error_word() (which allocates nothing either: the error words are a static device array too) and
+// cleared with xtb_error_clear().
 //
 // Limits and sharing: at most XTB_NOALLOC_MAX_ROWS rows (16 images of 1025 tokens; 131 KB of row statistics).
 // Every GPU that loads the library holds the array until the process exits. All calls on a device share it and it
-// keeps the last call's contents: the row statistics are fully rewritten by every call and the status word is
-// cleared at the start of every call. Calls whose work overlaps on the GPU (different streams, or host threads
-// racing on one device) race on the array and must be serialised by the caller.
+// keeps the last call's contents: every call rewrites the statistics of all the rows it uses before reading them.
+// Calls whose work overlaps on the GPU (different streams, or host threads racing on one device) race on the array
+// and must be serialised by the caller.
 //
 // Set-up: the first call on a device, with that device current, looks up the array's device address
 // (cudaGetSymbolAddress), and the GEMM launcher sets its kernel's shared-memory attribute and reads how many CTAs
@@ -29,7 +32,6 @@ using namespace xtb;
 namespace {
 
 struct NoAllocScratch {
-    uint32_t status[64];                      // bounded-wait failures of the last call (256 bytes)
     float2 ms[XTB_NOALLOC_MAX_ROWS];          // per-row (mean, rstd) over the 2730 SwiGLU units
 };
 
@@ -108,9 +110,10 @@ extern "C" int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, co
     if (make_operand(&A, h8, rows, HIDP, A_BOX_ROWS) || make_operand(&W.op, w, D, HIDP, weight_box_rows(W_FC2)) ||
         resid_map(&xm, (__half *)x, rows))
         return -1;
-    XTB_CK(cudaMemsetAsync(sc->status, 0, sizeof(sc->status), st));
+    uint32_t *err = error_word(dev);
+    if (!err) return -1;
     k_rowstat_into<<<(rows + 255) / 256, 256, 0, st>>>((const float2 *)stat, sc->ms, rows);
     XTB_CK(cudaGetLastError());
-    if (launch_fc2_gemm(A, W, ascale, rows, xm, sc->ms, c, d, sc->status, st)) return -1;
+    if (launch_fc2_gemm(A, W, ascale, rows, xm, sc->ms, c, d, err, st)) return -1;
     return 0;
 }

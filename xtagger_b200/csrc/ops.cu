@@ -487,6 +487,27 @@ int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, _
     return run_gemm_sp<SpResid<true>>(w, h8, rows, ascale, p, st, &xm);
 }
 
+// The E4M3 encoders every epilogue uses, over a whole array: pairs through e4m3x2 (or, with via_f16, through the
+// attention output's fp16 staging, e4m3x2_via_f16), one pair per thread, a last odd element paired with 0.
+__global__ void k_e4m3_encode(const float *__restrict__ x, uint8_t *__restrict__ y, size_t n, int via_f16)
+{
+    const size_t i = 2 * ((size_t)blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= n) return;
+    const float a = x[i], b = i + 1 < n ? x[i + 1] : 0.f;
+    const uint32_t w = via_f16 ? e4m3x2_via_f16(a, b) : e4m3x2(a, b);
+    y[i] = (uint8_t)w;
+    if (i + 1 < n) y[i + 1] = (uint8_t)(w >> 8);
+}
+
+int launch_e4m3_encode(const float *x, uint8_t *y, size_t n, int via_f16, cudaStream_t st)
+{
+    if (!n) return 0;
+    const size_t pairs = (n + 1) / 2;
+    k_e4m3_encode<<<(unsigned)((pairs + 255) / 256), 256, 0, st>>>(x, y, n, via_f16);
+    XTB_CK(cudaGetLastError());
+    return 0;
+}
+
 int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t st)
 {
     if (K <= 0 || (K & 7) || rows <= 0 || ((uintptr_t)x & 15)) {
@@ -533,8 +554,8 @@ int launch_head_e4m3(const Weight8 &hw, const Operand &pn8, float ascale, int ni
 int prepare_kernels()
 {
     const int dev = current_device();
-    if (!error_word(dev) || num_sms(dev) <= 0) {  // lazily created per device: never inside a capture
-        fprintf(stderr, "eva: cannot set up the error word on device %d\n", dev);
+    if (!error_word(dev) || num_sms(dev) <= 0) {  // address looked up once per device: never inside a capture
+        fprintf(stderr, "eva: cannot look up the error word on device %d\n", dev);
         return -1;
     }
     const void *single[] = {(const void *)k_gemm<EpiPatch, 256, true, false, false>};

@@ -142,6 +142,7 @@ int launch_px_head(const __half *x, int nimg, const float *w, const float *b, co
 
 // Per-column max |x| of an fp16 [rows][K] tensor folded into amax (fp32, K a multiple of 8).
 int launch_amax_f16(const __half *x, int K, int rows, float *amax, cudaStream_t st);
+int launch_e4m3_encode(const float *x, uint8_t *y, size_t n, int via_f16, cudaStream_t st);
 
 // Failure-path self-test: a wait of at most timeout_us on a barrier that is (arrive) or is not arrived on.
 int launch_selftest_wait(uint32_t timeout_us, int arrive, cudaStream_t st);

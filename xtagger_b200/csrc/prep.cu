@@ -12,9 +12,11 @@
 //   4. fp16 (round to nearest even), BGR planes, patch-operand layout: pixel (i, j) channel plane q at patch
 //      (i / 14) * 32 + j / 14, column q * 196 + (i % 14) * 14 + j % 14; columns 588..591 zero.
 // The arithmetic is the reference's operation for operation: integer steps exactly, the filter weights with one
-// rounding per operation in source order (explicit _rn intrinsics, so nothing is contracted into an FMA), and the
-// two passes as chains of fused multiply-adds in tap order, as the reference's _mm256_fmadd_ps / _mm_fmadd_ps. The
-// outputs are therefore bit-identical to a faithful CPU restatement of procimg.h.
+// rounding per operation in source order (explicit _rn intrinsics, so the compiler fuses nothing on its own) and a
+// fused multiply-add exactly where the reference's release build has one (the products GCC -O3 contracts in
+// pi_cubic and pi_axis), and the two passes as chains of fused multiply-adds in tap order, as the reference's
+// _mm256_fmadd_ps / _mm_fmadd_ps. The outputs are bit-identical to procimg.h's own functions compiled with the
+// reference's flags (tests/golden/golden_prep.json).
 //
 // Kernels (all HBM / L2-bound byte and fp32 work): k_over_white (one pixel per thread), k_half (one output pixel per
 // thread), k_axis (one output index per thread, both axes), k_vpass (one source pixel of one output row per thread:
@@ -64,12 +66,13 @@ __global__ void k_half(const uint8_t *s, int sstride, uint8_t *d, int wn, int ds
     *(uint32_t *)(d + (size_t)y * dstride + 4 * x) = o;
 }
 
-// Keys bicubic, a = -0.5 (pi_cubic), one rounding per operation
+// Keys bicubic, a = -0.5 (pi_cubic), as the reference's release build evaluates it (GCC -O3 with FMA contracts every
+// product that feeds one add): fma(fma(1.5, x, -2.5) x, x, 1) and a chain of three fused multiply-adds.
 __device__ __forceinline__ float cubic_rn(float x)
 {
     x = fabsf(x);
-    if (x < 1.0f) return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(__fmul_rn(1.5f, x), 2.5f), x), x), 1.0f);
-    if (x < 2.0f) return __fadd_rn(__fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(__fmul_rn(-0.5f, x), 2.5f), x), 4.0f), x), 2.0f);
+    if (x < 1.0f) return __fmaf_rn(__fmul_rn(__fmaf_rn(1.5f, x, -2.5f), x), x, 1.0f);
+    if (x < 2.0f) return __fmaf_rn(__fmaf_rn(__fmaf_rn(-0.5f, x, 2.5f), x, -4.0f), x, 2.0f);
     return 0.0f;
 }
 
@@ -112,7 +115,7 @@ __global__ void k_axis(AxisArgs ax, AxisArgs ay)
     for (int j = 0; j < b - a; j++) wi[j] = __fmul_rn(wi[j], sum);
     A.s[i] = a - A.off;
     A.n[i] = b - a;
-    A.k[i] = __fadd_rn(__fmul_rn(__fmul_rn(255.0f, white), sum), A.add);
+    A.k[i] = __fmaf_rn(__fmul_rn(255.0f, white), sum, A.add);  // contracted in the reference's build, as cubic_rn
 }
 
 // Vertical pass for output row blockIdx.y: tmp[i][4 px + c] = k[i] + sum_j w[i][j] src[s[i] + j][px][c] (FMA chain)

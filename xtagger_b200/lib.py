@@ -101,6 +101,7 @@ _SIGS = {
     "xtb_head_e4m3": (C.c_int, [_P, C.c_int, _P, _P, C.c_int, C.c_float, _P, _P, _P]),
     "xtb_fc2_noalloc": (C.c_int, [_P, C.c_int, _P, _P, C.c_float, _P, _P, _P, _P, _P]),
     "xtb_amax_f16": (C.c_int, [_P, C.c_int, C.c_int, _P, _P]),
+    "xtb_e4m3_encode": (C.c_int, [_P, _P, C.c_size_t, C.c_int, _P]),
     "xtb_sparse24_check": (C.c_int, [_P, C.c_int, C.c_int]),
     "xtb_sparse24_compress": (C.c_int, [_P, C.c_int, C.c_int, _P, _P]),
     "xtb_gemm_sp_e4m3_f32": (C.c_int, [_P, C.c_int, C.c_int, _P, _P, C.c_int, _P, C.c_float, _P, _P]),

@@ -118,6 +118,27 @@ def synthetic_inputs(n, seed=1):
     return np.stack([patch_operand(rng.random((448, 448, 3), dtype=np.float32)) for _ in range(n)]).view(np.uint16)
 
 
+def structured_image(rng, side=448, grid=8, amp=0.25, noise=0.05):
+    """One seeded synthetic image with image-level content, RGB in [0, 1]: a base colour U[0.15, 0.85] per channel,
+    a smooth field (N(0, 1) on a grid x grid lattice, bilinearly interpolated) times amp, and N(0, noise) pixel
+    noise, clipped. Unlike uniform-noise pixels, the token mean of such an image differs from image to image."""
+    base = rng.uniform(0.15, 0.85, 3)
+    g = rng.standard_normal((grid, grid, 3))
+    t = np.clip((np.arange(side) + 0.5) * grid / side - 0.5, 0, grid - 1)
+    i0 = np.minimum(t.astype(np.int64), grid - 2)
+    w = (t - i0)[:, None]
+    rows = g[i0] * (1 - w)[:, :, None] + g[i0 + 1] * w[:, :, None]                       # [side][grid][3]
+    field = rows[:, i0] * (1 - w.T)[:, :, None] + rows[:, i0 + 1] * w.T[:, :, None]      # [side][side][3]
+    img = base + amp * field + noise * rng.standard_normal((side, side, 3))
+    return np.clip(img, 0, 1).astype(np.float32)
+
+
+def structured_inputs(n, seed=1):
+    """n seeded structured_image()s as patch operands, uint16 view [n][1024][592]."""
+    rng = np.random.default_rng(seed)
+    return np.stack([patch_operand(structured_image(rng)) for _ in range(n)]).view(np.uint16)
+
+
 class _Blob:
     def __init__(self):
         self.parts, self.n = [], 0
