@@ -22,9 +22,12 @@ Prints one JSON line (rank 0):
               engine's stream, max over ranks);
   e2e         the same metric through the engine's public calls (eva_submit / eva_wait) with host buffers: every
               step copies its inputs from a pinned host pool and its scores back (wall clock, max over ranks);
-  roofline    the dominant kernel (fc1, 38 % of the FLOPs): algorithmic FLOPs per launch over its average launch
-              time from one direct (non-graph) forward timed with events on the launching stream, against the
-              FP8 dense peak taken as 2x the measured bf16 peak;
+  roofline    the dominant kernel by time, attention (36 % of the step): algorithmic FLOPs per launch over its
+              average launch time from one direct (non-graph) forward timed with events on the launching stream,
+              against the FP8 dense peak taken as 2x the measured bf16 peak, with its exp2 count and the floor those
+              exponentials set on the MUFU unit; roofline_fc1 the same for fc1 (38 % of the FLOPs);
+  free_scales   the resident forward on max / 448 block scales (the promoting kernels), single GPU;
+  gemm_config1  BASELINE config 1 (1025 x 2730 x 1024 block-scaled E4M3 GEMM) cold, single GPU;
   cpu_baseline  the CPU oracle (plain C, OpenMP) on a bounded sample, rank 0 at N = 1.
 --impl reference times the CPU restatement of the reference's forward (the reference has no CPU path of its
 own and its host engine is Windows-only) on the same config and prints the same line with "impl": "reference".
@@ -50,6 +53,13 @@ FC1_FLOP_PER_ROW = 2.0 * 5472 * 1024
 # 87.2 MB in the same capture, within 1 % of this, so the figure stands for the dense fc1 under every scale format.
 FC1_TRAFFIC_PER_ROW = (39.4752e6 + 48.742912e6) / (32 * 1025)
 FLOP_PER_IMAGE = 723.5e9
+# attention per layer and image: QK^T and PV over 16 heads of 64 (2 x 2 x 1025^2 x 64 x 16 FLOPs), one exp2 per score
+# (16 x 1025^2), algorithmic bytes = q8 / k8 / v8 read once (3 x 16 x 1025 x 64) + the E4M3 output (1025 x 1024);
+# DRAM bytes per image from the ncu capture of k_attention at batch 32 (109.09 MB read + 15.34 MB written).
+ATT_FLOP_PER_IMAGE = 4.0 * 1025 * 1025 * 64 * 16
+ATT_EXP_PER_IMAGE = 16.0 * 1025 * 1025
+ATT_BYTES_PER_IMAGE = 3.0 * 16 * 1025 * 64 + 1025 * 1024
+ATT_TRAFFIC_PER_IMAGE = (109.09e6 + 15.34e6) / 32
 
 
 from xtagger_b200.clocks import Clocks  # noqa: E402
@@ -88,6 +98,93 @@ def cpu_sample(model, nimg=1):
     O.forward(model, x)   # the reference's attention tiling (64-key tiles, 16-row slices)
     dt = time.perf_counter() - t0
     return nimg / dt, cores, dt
+
+
+def num_sms():
+    import torch
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+
+
+def time_free_scales(args, pool, nb, local, steps=5, warmup=3):
+    """The same device-resident forward on weights whose 128 x 128 block scales are max / 448 (the quantiser's natural
+    output) instead of powers of two: every projection then promotes its 128-deep K blocks in the epilogue."""
+    import torch
+    from xtagger_b200 import model as M
+    from xtagger_b200.engine import Engine
+    d = os.environ.get("XTB_BENCH_DIR", os.path.join(tempfile.gettempdir(), "xtb_bench"))
+    kw = dict(MODEL_KW, pow2=False)
+    eng = Engine(M.cached_synthetic(d, **kw), devices=(local,), nb=nb)
+    try:
+        eng.ready()
+        eng.upload(pool)
+        st = torch.cuda.ExternalStream(eng.stream(0), device=torch.device("cuda", local))
+        for _ in range(warmup):
+            eng.forward_resident()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            eng.forward_resident()
+        e1.record(st)
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3
+        return {"value": nb * steps / t, "unit": "images/s", "steps": steps, "block_scale_kinds":
+                eng.block_scale_kinds(), "weights": "random-init, E4M3 with fp32 scales per 128x128 block (max / 448)"}
+    finally:
+        eng.close()
+
+
+def time_gemm_config1(local, reps=50):
+    """BASELINE config 1 on the device through xtb_gemm_e4m3_f32: A [1025][1024] ~ N(0, 1) in E4M3 with one scale
+    max|A| / 448, W [2730][1024] ~ N(0, 0.02) in E4M3 with fp32 scales per 128 x 128 block (max / 448), fp32 out, seed
+    0. Cold: L2 flushed (a 256 MB write) before every launch; each launch timed alone with CUDA events. Error against
+    a float64 dequantise-then-matmul in PyTorch."""
+    import numpy as np
+    import torch
+    from xtagger_b200 import lib as XL
+    from xtagger_b200 import model as M
+    dev = torch.device("cuda", local)
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((1025, 1024), dtype=np.float32)
+    ascale = float(np.abs(a).max()) / 448.0
+    a8 = M._e4m3(a / ascale)
+    w8, ws = M.quant_blocks(rng.standard_normal((2730, 1024), dtype=np.float32) * 0.02)
+    da, dw, dws = (torch.from_numpy(np.ascontiguousarray(v)).to(dev) for v in (a8, w8, ws))
+    out = torch.empty((1025, 2730), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    xl = XL.lib()
+    st = torch.cuda.current_stream(dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def launch():
+        XL.check(xl.xtb_gemm_e4m3_f32(P(da), 1025, 1024, P(dw), 2730, P(dws), ascale, P(out),
+                                      ctypes.c_void_p(st.cuda_stream)), "xtb_gemm_e4m3_f32")
+    for _ in range(5):
+        launch()
+    times = []
+    for _ in range(reps):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        launch()
+        e1.record(st)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    us = float(np.median(times))
+    ref = (torch.from_numpy(M.e4m3_decode(a8).astype(np.float64) * ascale).to(dev) @
+           torch.from_numpy(M.dequant_blocks(w8, ws).astype(np.float64)).to(dev).T)
+    err = float((out.double() - ref).abs().max() / ref.abs().max())
+    flop, nbytes = 2.0 * 1025 * 1024 * 2730, 1025 * 1024 + 2730 * 1024 + ws.size * 4 + 1025 * 2730 * 4
+    hbm = None
+    try:
+        hbm = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        pass
+    return {"cold_us_median": us, "cold_us_min": float(min(times)), "tflops": flop / (us * 1e-6) / 1e12,
+            "gb_per_s": nbytes / (us * 1e-6) / 1e9, "hbm_frac": (nbytes / (us * 1e-6) / 1e9 / hbm) if hbm else None,
+            "algorithmic_bytes": nbytes, "max_abs_err_over_max_abs_ref": err,
+            "what": "1025x2730x1024 E4M3 block-scaled GEMM, fp32 out, L2 flushed before each of the timed launches, "
+                    "median of " + str(reps)}
 
 
 def run_reference(args, rank, world):
@@ -247,18 +344,48 @@ def run_ours(args, rank, world, local):
                            "antialiased bicubic 896 -> 448; quadrants: normalise) -> forward -> scores D2H, CUDA "
                            "events on the engine stream, max over ranks"}
 
-    # ---- roofline of the dominant kernel (fc1) from one direct forward with per-kernel events ----
+    # ---- rooflines from one direct (non-graph) forward with per-kernel events on the engine's stream: attention, the
+    # dominant kernel by time, and fc1, the dominant one by FLOPs ----
     prof = eng.profile()
     sparse_kinds = eng.sparse_kinds()
     block_scale_kinds = eng.block_scale_kinds()
     fc1_sparse = bool(sparse_kinds & 4)
-    fc1_ms = prof["fc1"] / 24
     rows = nb * 1025
-    achieved = FC1_FLOP_PER_ROW * rows / (fc1_ms * 1e-3) / 1e12   # dense-equivalent FLOPs
     bf16, peak_src = peaks()
-    peak = (4 if fc1_sparse else 2) * bf16
+    fc1_ms = prof["fc1"] / 24
+    achieved = FC1_FLOP_PER_ROW * rows / (fc1_ms * 1e-3) / 1e12   # dense-equivalent FLOPs
+    fc1_peak = (4 if fc1_sparse else 2) * bf16
+    fc1_src = peak_src
     if fc1_sparse:
-        peak_src = peak_src.replace("2x", "4x") + "; 2:4-sparse FP8 runs at twice the dense FP8 rate"
+        fc1_src = peak_src.replace("2x", "4x") + "; 2:4-sparse FP8 runs at twice the dense FP8 rate"
+    att_ms = prof["attention"] / 24
+    att_flop = ATT_FLOP_PER_IMAGE * nb
+    att_exp = ATT_EXP_PER_IMAGE * nb
+    sm_mhz = clocks.get("sm_mhz") or 1965.0
+    exp_floor_ms = att_exp / (16 * num_sms() * sm_mhz * 1e6) * 1e3   # every exponential on the MUFU unit
+    roof_att = {"bound": "tensor", "kernel": "attention (k_attention + k_attention_last: tcgen05 QK^T / PV, "
+                "exp2 softmax, E4M3 P)", "achieved": att_flop / (att_ms * 1e-3) / 1e12, "peak": 2 * bf16,
+                "unit": "TFLOP/s", "frac": att_flop / (att_ms * 1e-3) / 1e12 / (2 * bf16), "peak_source": peak_src,
+                "flop_per_launch": att_flop, "launch_ms": att_ms,
+                "traffic": ATT_TRAFFIC_PER_IMAGE * nb,
+                "traffic_unit": "bytes per launch (ncu DRAM read + write at batch 32, scaled by images)",
+                "algorithmic_bytes": ATT_BYTES_PER_IMAGE * nb,
+                "exp2_per_launch": att_exp, "exp2_floor_ms": exp_floor_ms,
+                "frac_of_exp2_floor": exp_floor_ms / att_ms,
+                "exp2_floor_source": f"16 exp2 per clock per SM x {num_sms()} SMs at the median SM clock {sm_mhz:.0f} MHz"}
+    roof_fc1 = {"bound": "tensor",
+                "kernel": "fc1 (tcgen05.mma.sp 2:4-sparse E4M3 GEMM + SwiGLU epilogue)" if fc1_sparse
+                else "fc1 (tcgen05 E4M3 GEMM + SwiGLU epilogue)",
+                "achieved": achieved, "peak": fc1_peak, "unit": "TFLOP/s", "frac": achieved / fc1_peak,
+                "peak_source": fc1_src, "flop_per_launch": FC1_FLOP_PER_ROW * rows, "launch_ms": fc1_ms,
+                "traffic": None if fc1_sparse else FC1_TRAFFIC_PER_ROW * rows,
+                "traffic_unit": "bytes per launch (ncu DRAM read + write at batch 32, scaled by rows)"}
+    free_scales = None
+    if rank == 0 and world == 1 and not args.no_extra and not (args.v3 or args.free_scales or args.sparse or args.mix):
+        free_scales = time_free_scales(args, pool, nb, local)
+    gemm1 = None
+    if rank == 0 and world == 1 and not args.no_extra:
+        gemm1 = time_gemm_config1(local)
     out = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, dt = cpu_sample(model, nimg=4)
@@ -284,14 +411,14 @@ def run_ours(args, rank, world, local):
                            "l2": "no flush: the working set per step (0.33 GB weights + activations) exceeds L2"},
                 "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": args.batch * 1024 * 592 * 2,
                         "d2h_bytes_per_step": args.batch * args.nt * 4},
-                "roofline": {"bound": "tensor",
-                             "kernel": "fc1 (tcgen05.mma.sp 2:4-sparse E4M3 GEMM + SwiGLU epilogue)" if fc1_sparse
-                             else "fc1 (tcgen05 E4M3 GEMM + SwiGLU epilogue)",
-                             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                             "peak_source": peak_src, "flop_per_launch": FC1_FLOP_PER_ROW * rows,
-                             "launch_ms": fc1_ms,
-                             "traffic": None if fc1_sparse else FC1_TRAFFIC_PER_ROW * rows,
-                             "traffic_unit": "bytes per launch (ncu DRAM read + write at batch 32, scaled by rows)"},
+                "roofline": roof_att,
+                "roofline_fc1": roof_fc1,
+                "value_clock_normalised": (value * clocks["sm_max_mhz"] / clocks["sm_mhz"]
+                                           if clocks.get("sm_mhz") and clocks.get("sm_max_mhz") else None),
+                "value_clock_normalised_how": "value x max SM clock / median SM clock during the timed region (for "
+                                              "comparing runs at different clocks, e.g. across GPU counts)",
+                "free_scales": free_scales,
+                "gemm_config1": gemm1,
                 "forward_tflops": FLOP_PER_IMAGE * value / 1e12,
                 "e2e_decoded": decoded,
                 "profile_ms": prof,
@@ -328,6 +455,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=None, help="global batch (default 64; 128 with --sparse)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the extra single-GPU keys (free_scales forward, config-1 GEMM)")
     ap.add_argument("--nt", type=int, default=NT, help="head size (tags): 10861, or 13461 for the PixAI-style config")
     ap.add_argument("--sparse", action="store_true", help="config 5: 2:4-pruned projections on the sparse kernels")
     ap.add_argument("--v3", action="store_true", help="weights in the reference's v3 format (per-tensor scales)")

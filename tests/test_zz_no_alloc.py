@@ -8,9 +8,10 @@ partials; xtb_fc2_noalloc leaves them untouched and keeps that scratch in a stat
 Checked on two calls in a row (the second with fewer rows, so a stale tail of the shared array from the first call
 would show): bit-identical to xtb_fc2 (the same GEMM launch, and row statistics summed in the same order), within the
 fc2 tolerance of the oracle, the library's error word still 0 (a bounded wait that runs out inside the call would
-set it), the caller's partials unchanged. In a fresh process whose CUDA modules are loaded eagerly (so that loading
-the library's code cannot be mistaken for an allocation), free device memory is the same before the first call and
-after two calls. Collected last, so that a run stopping at the first failure has run every other test."""
+set it), the caller's partials unchanged. In a fresh process whose CUDA modules are loaded eagerly, and after one
+unrelated library call has loaded the library's code and static arrays (so that loading them cannot be mistaken for
+an allocation), free device memory is the same before the first call and after two calls. Collected last, so that a
+run stopping at the first failure has run every other test."""
 import os
 import subprocess
 import sys
@@ -95,6 +96,9 @@ st = torch.ones((43, rows, 2), dtype=torch.float32, device=dev)
 c = torch.zeros(1024, dtype=torch.float32, device=dev)
 d = torch.zeros(1024, dtype=torch.float32, device=dev)
 P = lambda t: C.c_void_p(t.data_ptr())
+# the library links its own CUDA runtime: its first CUDA call of any kind loads all of the library's code and static
+# device arrays onto the device (eagerly here); make that call outside the measured window
+assert xl.xtb_error_word(0) == 0
 torch.cuda.synchronize()
 free0 = torch.cuda.mem_get_info(0)[0]
 for _ in range(2):
