@@ -17,6 +17,32 @@
 
 namespace xtb {
 
+// (mean, rstd) over the 2730 SwiGLU units of a row from fc1's NSTAT partial (sum, sum of squares) pairs, four threads
+// per row (lanes 4 i .. 4 i + 3 of a warp: `row`, part j = lane & 3): part j adds partials j, j + 4, ... in order, and
+// the four part sums are combined as (t0 + t1) + (t2 + t3) by two butterfly shuffles. Addition commutes, so every lane
+// of the four gets the same bits: a fixed order, whatever the schedule. All 32 lanes of the warp must call it.
+__device__ __forceinline__ float2 rowstat_of(const float2 *__restrict__ stat, int rows, int row, int j)
+{
+    float s = 0.f, q = 0.f;
+    if (row < rows) {
+#pragma unroll
+        for (int g = j; g < NSTAT; g += 4) {
+            const float2 v = stat[(size_t)g * rows + row];
+            s += v.x;
+            q += v.y;
+        }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    q += __shfl_xor_sync(0xffffffffu, q, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    q += __shfl_xor_sync(0xffffffffu, q, 2);
+    const float mean = s * (1.0f / HID);
+    return make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
+}
+constexpr int ROWSTAT_THREADS = 256;  // 64 rows per block
+__host__ __device__ constexpr int rowstat_blocks(int rows) { return (rows * 4 + ROWSTAT_THREADS - 1) / ROWSTAT_THREADS; }
+
+
 // ---- QKV projection: acc = x W_qkv^T (dequantised); columns [0,1024) q, [1024,2048) k, [2048,3072) v ----
 // q, k: scaled by cq / ck, interleaved RoPE (pair (2j, 2j+1) of a head shares angle j, table cs[t - 1][j] =
 // (cos, sin)) for patch tokens t >= 1; v: scaled by cv. E4M3 -> q8 / k8 / v8 [img][head][TP][64] (row t of 64
@@ -45,6 +71,7 @@ struct EpiQKV {
     {
         uint8_t *st = cx.stage + h * 4096;
         const int t0 = cx.row0 % T;
+        float4 vv[8];  // all loads first, then the staging stores
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int r = 4 * i + (cx.lane >> 3), c = cx.lane & 7;
@@ -52,8 +79,10 @@ struct EpiQKV {
             if (tt >= T) tt -= T;
             float4 v = make_float4(1.f, 0.f, 1.f, 0.f);  // cls rows and rows past M: identity
             if (tt > 0 && cx.row0 + r < p.M) v = __ldg((const float4 *)(p.cs + (size_t)(tt - 1) * 32 + 16 * h) + c);
-            *(float4 *)stage_chunk(st, r, c) = v;
+            vv[i] = v;
         }
+#pragma unroll
+        for (int i = 0; i < 8; i++) *(float4 *)stage_chunk(st, 4 * i + (cx.lane >> 3), cx.lane & 7) = vv[i];
     }
     // Both halves are staged before the accumulator is built (the staging buffer is free between tiles: the
     // previous tile's stores read it synchronously), so those loads overlap the main loop.
@@ -117,15 +146,20 @@ struct EpiQKV {
             for (int q = 0; q < 4; q++) *(uint4 *)stage_chunk(cx.stage, cx.lane, 4 * hh + q) = o[hh][q];
         __syncwarp();
         uint8_t *dst = which == 0 ? p.q8 : which == 1 ? p.k8 : p.v8;
+        uint4 pieces[8];  // all staged pieces first, then the stores (see EpiF32::apply)
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int pc = i * 32 + cx.lane;          // piece: head hh, row r, 16-byte chunk ch
+            pieces[i] = *(const uint4 *)stage_chunk(cx.stage, (pc >> 2) & 31, 4 * (pc >> 7) + (pc & 3));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int pc = i * 32 + cx.lane;
             const int hh = pc >> 7, r = (pc >> 2) & 31, ch = pc & 3;
             const int rw = cx.row0 + r;
             if (rw < p.M) {
                 const int bb = rw / T, tt = rw - bb * T;
-                *(uint4 *)(dst + (((size_t)(bb * NH + head0 + hh) * TP + tt) << 6) + ch * 16) =
-                    *(const uint4 *)stage_chunk(cx.stage, r, 4 * hh + ch);
+                *(uint4 *)(dst + (((size_t)(bb * NH + head0 + hh) * TP + tt) << 6) + ch * 16) = pieces[i];
             }
         }
         __syncwarp();
@@ -276,12 +310,15 @@ struct EpiPatch {
             __syncwarp();
             const int w = (cx.lane & 15) * 2;
             const int col = cx.col0 + 32 * c + w;
+            float2 sv[16];  // all staged values first, then the loads of pos and the stores (see EpiF32::apply)
+#pragma unroll
+            for (int i = 0; i < 16; i++) sv[i] = stage_f32x2(cx.stage, 2 * i + (cx.lane >> 4), w);
 #pragma unroll 4
             for (int i = 0; i < 16; i++) {
                 const int r = 2 * i + (cx.lane >> 4), rw = cx.row0 + r;
                 if (rw < p.M) {
                     const int b = rw >> 10, pp = rw & 1023;
-                    const float2 a = stage_f32x2(cx.stage, r, w);
+                    const float2 a = sv[i];
                     const float2 ps = *(const float2 *)(p.pos + (size_t)(1 + pp) * D + col);
                     const float2 ah = __half22float2(__floats2half2_rn(a.x, a.y));
                     *(__half2 *)(p.x + ((size_t)b * T + 1 + pp) * D + col) = __floats2half2_rn(ah.x + ps.x, ah.y + ps.y);

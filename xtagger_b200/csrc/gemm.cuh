@@ -326,13 +326,17 @@ struct EpiF32 {
             __syncwarp();
             stage_row_f32(cx.stage, cx.lane, acc + 32 * c);
             __syncwarp();
+            // every staged value into registers first, then the stores back to back: a staging load issued after a
+            // global store through a pointer the compiler cannot tell apart from it is ordered behind that store,
+            // which made the warp wait out each store's latency in turn
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = stage_f32(cx.stage, i, cx.lane);
             const int col = cx.col0 + 32 * c + cx.lane;
             if (col < p.N) {
-#pragma unroll 4
-                for (int i = 0; i < 32; i++) {
-                    const int row = cx.row0 + i;
-                    if (row < p.M) p.out[(size_t)row * p.ld + col] = stage_f32(cx.stage, i, cx.lane);
-                }
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (cx.row0 + i < p.M) p.out[(size_t)(cx.row0 + i) * p.ld + col] = v[i];
             }
         }
         __syncwarp();

@@ -39,20 +39,14 @@ struct NoAllocScratch {
 // cudaGetSymbolAddress for the current device, never the name itself.
 static __device__ __align__(256) NoAllocScratch g_noalloc;
 
-// (mean, rstd) of every row from fc1's NSTAT partials, summed in a fixed order (as k_rowstat), into ms.
-__global__ void __launch_bounds__(256) k_rowstat_into(const float2 *__restrict__ stat, float2 *__restrict__ ms, int rows)
+// (mean, rstd) of every row from fc1's NSTAT partials into ms, four threads per row in the fixed order of k_rowstat
+// (the same rowstat_of), so that the result is bit-identical to xtb_fc2's.
+__global__ void __launch_bounds__(ROWSTAT_THREADS) k_rowstat_into(const float2 *__restrict__ stat, float2 *__restrict__ ms,
+                                                                  int rows)
 {
-    const int row = blockIdx.x * 256 + threadIdx.x;
-    if (row >= rows) return;
-    float s = 0.f, q = 0.f;
-#pragma unroll 4
-    for (int g = 0; g < NSTAT; g++) {
-        const float2 v = stat[(size_t)g * rows + row];
-        s += v.x;
-        q += v.y;
-    }
-    const float mean = s * (1.0f / HID);
-    ms[row] = make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
+    const int t = blockIdx.x * ROWSTAT_THREADS + threadIdx.x, row = t >> 2;
+    const float2 v = rowstat_of(stat, rows, row, t & 3);
+    if ((t & 3) == 0 && row < rows) ms[row] = v;
 }
 
 struct DeviceScratch {
@@ -112,7 +106,7 @@ extern "C" int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, co
         return -1;
     uint32_t *err = error_word(dev);
     if (!err) return -1;
-    k_rowstat_into<<<(rows + 255) / 256, 256, 0, st>>>((const float2 *)stat, sc->ms, rows);
+    k_rowstat_into<<<rowstat_blocks(rows), ROWSTAT_THREADS, 0, st>>>((const float2 *)stat, sc->ms, rows);
     XTB_CK(cudaGetLastError());
     if (launch_fc2_gemm(A, W, ascale, rows, xm, sc->ms, c, d, err, st)) return -1;
     return 0;

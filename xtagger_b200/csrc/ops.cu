@@ -366,7 +366,7 @@ int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __ha
 {
     CUtensorMap xm;
     if (resid_map(&xm, x, rows)) return -1;
-    k_rowstat<<<(rows + 255) / 256, 256, 0, st>>>(stat, rows);
+    k_rowstat<<<rowstat_blocks(rows), ROWSTAT_THREADS, 0, st>>>((float2 *)stat, rows);
     XTB_CK(cudaGetLastError());
     return launch_fc2_gemm(h8, w, ascale, rows, xm, stat, c, d, nullptr, st);
 }
@@ -481,7 +481,7 @@ int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, _
 {
     CUtensorMap xm;
     if (sp_resid_map(&xm, x, rows)) return -1;
-    k_rowstat<<<(rows + 255) / 256, 256, 0, st>>>(stat, rows);
+    k_rowstat<<<rowstat_blocks(rows), ROWSTAT_THREADS, 0, st>>>((float2 *)stat, rows);
     XTB_CK(cudaGetLastError());
     SpResid<true>::Params p{stat, c, d, rows};
     return run_gemm_sp<SpResid<true>>(w, h8, rows, ascale, p, st, &xm);

@@ -40,13 +40,13 @@ struct EpiPxPatch {
             __syncwarp();
             const int w = (cx.lane & 15) * 2;
             const int col = cx.col0 + 32 * c + w;
-#pragma unroll 4
+            float2 sv[16];  // all staged values first, then the stores (see EpiF32::apply)
+#pragma unroll
+            for (int i = 0; i < 16; i++) sv[i] = stage_f32x2(cx.stage, 2 * i + (cx.lane >> 4), w);
+#pragma unroll
             for (int i = 0; i < 16; i++) {
-                const int r = 2 * i + (cx.lane >> 4), rw = cx.row0 + r;
-                if (rw < p.M) {
-                    const float2 a = stage_f32x2(cx.stage, r, w);
-                    *(__half2 *)(p.x + (size_t)rw * D + col) = __floats2half2_rn(a.x, a.y);
-                }
+                const int rw = cx.row0 + 2 * i + (cx.lane >> 4);
+                if (rw < p.M) *(__half2 *)(p.x + (size_t)rw * D + col) = __floats2half2_rn(sv[i].x, sv[i].y);
             }
         }
         __syncwarp();
@@ -73,6 +73,7 @@ struct EpiPxQKV {
     {
         uint8_t *st = cx.stage + h * 4096;
         const int t0 = cx.row0 % p.L;
+        float4 vv[8];  // all loads first, then the staging stores
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int r = 4 * i + (cx.lane >> 3), c = cx.lane & 7;
@@ -80,8 +81,10 @@ struct EpiPxQKV {
             if (tt >= p.L) tt -= p.L;
             float4 v = make_float4(1.f, 0.f, 1.f, 0.f);  // rows past M: identity
             if (cx.row0 + r < p.M) v = __ldg((const float4 *)(p.cs + (size_t)tt * 32 + 16 * h) + c);
-            *(float4 *)stage_chunk(st, r, c) = v;
+            vv[i] = v;
         }
+#pragma unroll
+        for (int i = 0; i < 8; i++) *(float4 *)stage_chunk(st, 4 * i + (cx.lane >> 3), cx.lane & 7) = vv[i];
     }
     __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &)
     {

@@ -130,19 +130,14 @@ __global__ void k_selftest_wait(uint64_t ns, int arrive, uint32_t *err)
 // wrote for a row are added in a fixed order (bit-identical run to run, as eva_kernels.cu:205-210) and turned into
 // (mean, rstd) over the 2730 units (eps 1e-6, k_fc2's formula, eva_kernels.cu:318-320), written in place into
 // partial 0 of the row.
-__global__ void __launch_bounds__(256) k_rowstat(float2 *__restrict__ stat, int rows)
+// Each row's (mean, rstd) into partial 0 of stat (consumed by fc2's epilogue). Four threads per row so that small
+// batches still spread the partial loads over the SMs.
+__global__ void __launch_bounds__(ROWSTAT_THREADS) k_rowstat(float2 *__restrict__ stat, int rows)
 {
-    const int row = blockIdx.x * 256 + threadIdx.x;
-    if (row >= rows) return;
-    float s = 0.f, q = 0.f;
-#pragma unroll 4
-    for (int g = 0; g < NSTAT; g++) {
-        const float2 v = stat[(size_t)g * rows + row];
-        s += v.x;
-        q += v.y;
-    }
-    const float mean = s * (1.0f / HID);
-    stat[row] = make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
+    const int t = blockIdx.x * ROWSTAT_THREADS + threadIdx.x, row = t >> 2;
+    const float2 ms = rowstat_of(stat, rows, row, t & 3);
+    __syncwarp();  // every part has read partial 0 of its row before part 0 overwrites it
+    if ((t & 3) == 0 && row < rows) stat[row] = ms;
 }
 
 // Mean over patch tokens 1..1024 of each image: x [img][1025][1024] fp16 -> pool [img][1024] fp32.
