@@ -272,6 +272,11 @@ typedef struct px {
 int px_open(px *p, const char *weights, int device, void *pool, size_t poolb);
 /* Same with nb inputs per submit (no counterpart in the reference, which fixes PX_NB). */
 int px_open_ex(px *p, const char *weights, int device, uint32_t nb, void *pool, size_t poolb);
+/* Same on ndev devices (no counterpart in the reference, which drives one GPU): one complete engine replica per
+ * device (weights copied to each), nb inputs per submit split into contiguous shards (sizes differ by at most one,
+ * at most 64 per device), each shard's forward on its own device and stream, the scores gathered into hout[buf] by
+ * px_wait. px_stream / px_input / px_profile / px_launches_per_forward report the first device's replica. */
+int px_open_multi(px *p, const char *weights, const int *devices, int ndev, uint32_t nb, void *pool, size_t poolb);
 int px_ready(px *p);                          /* px.h:386-397: join the bring-up; 0 or -1 */
 int px_poll(px *p);                           /* px.h:399-402: 1 once the bring-up has finished */
 /* Replaces px_submit (px.h:405-418): n <= nb inputs (PX_IN halves each; adjacent ones in one copy) into slot

@@ -43,6 +43,18 @@ def test_open_ex_argument_checks(xlib, tmp_path):
     assert xlib.eva_open_ex(C.byref(e), b"x.bin", devs, 4, 2, None, 0, 0) == -1      # batch < devices
 
 
+def test_px_open_multi_argument_checks(xlib):
+    from xtagger_b200 import lib as L
+    p = L.Px()
+    devs = (C.c_int * 9)(*range(9))
+    assert xlib.px_open_multi(C.byref(p), b"x.bin", devs, 9, 64, None, 0) == -1      # more than 8 devices
+    assert xlib.px_open_multi(C.byref(p), b"x.bin", devs, 0, 4, None, 0) == -1       # no device
+    assert xlib.px_open_multi(C.byref(p), b"x.bin", devs, 4, 2, None, 0) == -1       # batch < devices
+    assert xlib.px_open_multi(C.byref(p), b"x.bin", devs, 2, 129, None, 0) == -1     # more than 64 per device
+    assert xlib.px_open_multi(C.byref(p), b"x.bin", None, 2, 4, None, 0) == -1       # no device list
+    assert p.impl is None
+
+
 def test_prof_names(xlib):
     names = [xlib.eva_prof_name(i) for i in range(9)]
     assert all(names) and xlib.eva_prof_name(9) is None

@@ -9,6 +9,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <string>
 #include <thread>
 #include <vector>
@@ -62,7 +63,20 @@ struct PxImpl {
     cudaGraphExec_t graph = nullptr;
     cudaEvent_t done[PX_NBUF] = {};
     uint32_t *errh = nullptr;  // pinned, per slot: the device error word after the slot's forward
+    // several devices (px_open_multi): one complete single-device engine per device, each with its contiguous shard
+    // of every submit (shard i starts at input lo[i]); the scores are gathered into this handle's hout[buf]
+    std::vector<px> subs;
+    std::vector<uint32_t> lo;
+    uint32_t slot_n[PX_NBUF] = {};
+    bool multi() const { return !subs.empty(); }
 };
+
+// Inputs [lo, lo + nb) of a submit of n go to shard i: how many of them there are.
+uint32_t shard_n(const PxImpl *im, size_t i, uint32_t n)
+{
+    const uint32_t lo = im->lo[i];
+    return n > lo ? std::min(n - lo, im->subs[i].nb) : 0;
+}
 
 PxImpl *I(px *p) { return (PxImpl *)p->impl; }
 
@@ -324,6 +338,43 @@ int px_open_ex(px *p, const char *weights, int device, uint32_t nb, void *pool, 
     return 0;
 }
 
+int px_open_multi(px *p, const char *weights, const int *devices, int ndev, uint32_t nb, void *pool, size_t poolb)
+{
+    if (ndev == 1 && devices) return px_open_ex(p, weights, devices[0], nb, pool, poolb);
+    memset(p, 0, sizeof(*p));
+    if (!devices || ndev < 1 || ndev > 8 || nb < (uint32_t)ndev || nb > 64u * (uint32_t)ndev) {
+        fprintf(stderr, "px: %d devices with batch %u not supported (1..8 devices, 1..64 inputs per device)\n", ndev, nb);
+        return -1;
+    }
+    PxImpl *im = new PxImpl();
+    im->subs.resize(ndev);
+    im->lo.resize(ndev);
+    uint32_t lo = 0;
+    for (int i = 0; i < ndev; i++) {
+        const uint32_t ni = (nb + ndev - 1 - i) / ndev;  // contiguous shards, sizes differ by at most 1
+        im->lo[i] = lo;
+        // the caller's pool is page-locked once, by the first device's bring-up (portable: every device reads it)
+        if (px_open_ex(&im->subs[i], weights, devices[i], ni, i == 0 ? pool : nullptr, i == 0 ? poolb : 0)) {
+            for (int j = 0; j < i; j++) px_close(&im->subs[j]);
+            delete im;
+            return -1;
+        }
+        lo += ni;
+    }
+    p->impl = im;
+    p->nt = im->subs[0].nt;
+    p->ntp = im->subs[0].ntp;
+    p->nb = nb;
+    for (int s = 0; s < PX_NBUF; s++) {
+        p->hout[s] = (float *)aligned_alloc(4096, (((size_t)nb * p->nt * 4) + 4095) & ~(size_t)4095);
+        if (!p->hout[s]) {
+            px_close(p);
+            return -1;
+        }
+    }
+    return 0;
+}
+
 int px_open(px *p, const char *weights, int device, void *pool, size_t poolb)
 {
     return px_open_ex(p, weights, device, PX_NB, pool, poolb);
@@ -334,6 +385,13 @@ int px_ready(px *p)
     PxImpl *im = I(p);
     if (!im) return -1;
     if (im->up) return 0;
+    if (im->multi()) {
+        int rc = 0;
+        for (px &q : im->subs) rc |= px_ready(&q);  // join every bring-up, even after a failure
+        if (rc) return -1;
+        im->up = true;
+        return 0;
+    }
     if (im->boot_running) {
         im->boot.join();
         im->boot_running = false;
@@ -347,6 +405,11 @@ int px_ready(px *p)
 int px_poll(px *p)
 {
     PxImpl *im = I(p);
+    if (im && im->multi() && !im->up) {
+        for (px &q : im->subs)
+            if (!px_poll(&q)) return 0;
+        return 1;
+    }
     return im && (im->up || im->bstatus != -1 || !im->boot_running);
 }
 
@@ -354,6 +417,14 @@ int px_submit(px *p, uint32_t buf, uint16_t *const *in, uint32_t n)
 {
     if (px_ready(p) || buf >= PX_NBUF || n > p->nb) return -1;
     PxImpl *im = I(p);
+    if (im->multi()) {
+        for (size_t i = 0; i < im->subs.size(); i++) {
+            const uint32_t ni = shard_n(im, i, n);
+            if (ni && px_submit(&im->subs[i], buf, in + im->lo[i], ni)) return -1;
+        }
+        im->slot_n[buf] = n;
+        return 0;
+    }
     for (uint32_t i = 0, j; i < n; i = j) {
         for (j = i + 1; j < n && in[j] == in[j - 1] + PX_IN; j++)
             ;
@@ -371,6 +442,11 @@ int px_query(px *p, uint32_t buf)
 {
     PxImpl *im = I(p);
     if (!im || !im->up || buf >= PX_NBUF) return 1;
+    if (im->multi()) {
+        for (size_t i = 0; i < im->subs.size(); i++)
+            if (shard_n(im, i, im->slot_n[buf]) && !px_query(&im->subs[i], buf)) return 0;
+        return 1;
+    }
     return cudaEventQuery(im->done[buf]) != cudaErrorNotReady;
 }
 
@@ -378,6 +454,17 @@ const float *px_wait(px *p, uint32_t buf)
 {
     PxImpl *im = I(p);
     if (!im || !im->up || buf >= PX_NBUF) return nullptr;
+    if (im->multi()) {  // every shard's scores into its rows of this handle's slot
+        const float *ok = p->hout[buf];
+        for (size_t i = 0; i < im->subs.size(); i++) {
+            const uint32_t ni = shard_n(im, i, im->slot_n[buf]);
+            if (!ni) continue;
+            const float *r = px_wait(&im->subs[i], buf);
+            if (!r) ok = nullptr;
+            else memcpy(p->hout[buf] + (size_t)im->lo[i] * p->nt, r, (size_t)ni * p->nt * 4);
+        }
+        return ok;
+    }
     if (cudaEventSynchronize(im->done[buf]) != cudaSuccess) return nullptr;
     if (im->errh[buf]) {
         fprintf(stderr, "px: batch %u: device error word 0x%x (a bounded wait ran out)\n", buf, im->errh[buf]);
@@ -390,6 +477,13 @@ void px_close(px *p)
 {
     PxImpl *im = I(p);
     if (!im) return;
+    if (im->multi()) {
+        for (px &q : im->subs) px_close(&q);
+        for (int s = 0; s < PX_NBUF; s++) free(p->hout[s]);
+        delete im;
+        memset(p, 0, sizeof(*p));
+        return;
+    }
     if (im->boot_running) {
         im->boot.join();
         im->boot_running = false;
@@ -418,6 +512,11 @@ void px_close(px *p)
 int px_forward_resident(px *p)
 {
     if (px_ready(p)) return -1;
+    if (I(p)->multi()) {
+        for (px &q : I(p)->subs)
+            if (px_forward_resident(&q)) return -1;
+        return 0;
+    }
     ECK(cudaGraphLaunch(I(p)->graph, I(p)->st));
     return 0;
 }
@@ -426,6 +525,13 @@ int px_upload(px *p, uint16_t *const *in, uint32_t n)
 {
     if (px_ready(p) || n > p->nb) return -1;
     PxImpl *im = I(p);
+    if (im->multi()) {
+        for (size_t i = 0; i < im->subs.size(); i++) {
+            const uint32_t ni = shard_n(im, i, n);
+            if (ni && px_upload(&im->subs[i], in + im->lo[i], ni)) return -1;
+        }
+        return 0;
+    }
     for (uint32_t i = 0; i < n; i++)
         ECK(cudaMemcpyAsync(im->in + (size_t)i * PX_IN, in[i], PX_IN * 2, cudaMemcpyHostToDevice, im->st));
     ECK(cudaStreamSynchronize(im->st));
@@ -436,6 +542,13 @@ int px_download(px *p, float *out, uint32_t n)
 {
     if (px_ready(p) || n > p->nb) return -1;
     PxImpl *im = I(p);
+    if (im->multi()) {
+        for (size_t i = 0; i < im->subs.size(); i++) {
+            const uint32_t ni = shard_n(im, i, n);
+            if (ni && px_download(&im->subs[i], out + (size_t)im->lo[i] * p->nt, ni)) return -1;
+        }
+        return 0;
+    }
     ECK(cudaStreamSynchronize(im->st));
     ECK(cudaMemcpy(out, im->out, (size_t)n * p->nt * 4, cudaMemcpyDeviceToHost));
     return 0;
@@ -445,19 +558,31 @@ int px_head_input(px *p, uint16_t *o, uint32_t n)
 {
     if (px_ready(p) || n > p->nb) return -1;
     PxImpl *im = I(p);
+    if (im->multi()) {
+        for (size_t i = 0; i < im->subs.size(); i++) {
+            const uint32_t ni = shard_n(im, i, n);
+            if (ni && px_head_input(&im->subs[i], o + (size_t)im->lo[i] * D, ni)) return -1;
+        }
+        return 0;
+    }
     ECK(cudaStreamSynchronize(im->st));
     ECK(cudaMemcpy(o, im->o, (size_t)n * D * 2, cudaMemcpyDeviceToHost));
     return 0;
 }
 
-void *px_stream(px *p) { return px_ready(p) ? nullptr : (void *)I(p)->st; }
-void *px_input(px *p) { return px_ready(p) ? nullptr : (void *)I(p)->in; }
-int px_launches_per_forward(px *p) { return px_ready(p) ? -1 : I(p)->launches; }
+// with several devices: the first device's (its shard's inputs, its stream, its launches)
+void *px_stream(px *p) { return px_ready(p) ? nullptr : I(p)->multi() ? px_stream(&I(p)->subs[0]) : (void *)I(p)->st; }
+void *px_input(px *p) { return px_ready(p) ? nullptr : I(p)->multi() ? px_input(&I(p)->subs[0]) : (void *)I(p)->in; }
+int px_launches_per_forward(px *p)
+{
+    return px_ready(p) ? -1 : I(p)->multi() ? px_launches_per_forward(&I(p)->subs[0]) : I(p)->launches;
+}
 
 int px_profile(px *p, float *ms, int kinds)
 {
     if (px_ready(p)) return -1;
     PxImpl *im = I(p);
+    if (im->multi()) return px_profile(&im->subs[0], ms, kinds);  // the first device's shard
     for (int w = 0; w < 2; w++)
         if (forward(im, p, nullptr)) return -1;
     Prof pr;

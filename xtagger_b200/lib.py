@@ -45,6 +45,7 @@ _PX = C.POINTER(Px)
 _SIGS = {
     "px_open": (C.c_int, [_PX, C.c_char_p, C.c_int, _P, C.c_size_t]),
     "px_open_ex": (C.c_int, [_PX, C.c_char_p, C.c_int, C.c_uint32, _P, C.c_size_t]),
+    "px_open_multi": (C.c_int, [_PX, C.c_char_p, C.POINTER(C.c_int), C.c_int, C.c_uint32, _P, C.c_size_t]),
     "px_ready": (C.c_int, [_PX]),
     "px_poll": (C.c_int, [_PX]),
     "px_submit": (C.c_int, [_PX, C.c_uint32, C.POINTER(_P), C.c_uint32]),

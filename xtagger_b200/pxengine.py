@@ -13,15 +13,22 @@ PX_IN = L.PX_IN
 
 
 class PxEngine:
-    def __init__(self, weights, device=0, nb=L.PX_NB, pool=None):
-        """Open the engine on `device` with nb inputs per submit. `pool`: optional uint16 numpy array holding the
-        inputs (page-locked in place by the bring-up, like the reference's input pool)."""
+    def __init__(self, weights, device=0, nb=L.PX_NB, pool=None, devices=None):
+        """Open the engine on `device` (or on every device of `devices`, px_open_multi) with nb inputs per submit.
+        `pool`: optional uint16 numpy array holding the inputs (page-locked in place by the bring-up, like the
+        reference's input pool)."""
         self.lib = L.lib()
         self.p = L.Px()
         self.pool = pool
         pptr = pool.ctypes.data_as(C.c_void_p) if pool is not None else None
         pbytes = pool.nbytes if pool is not None else 0
-        L.check(self.lib.px_open_ex(C.byref(self.p), str(weights).encode(), device, nb, pptr, pbytes), "px_open_ex")
+        if devices is not None:
+            devs = (C.c_int * len(devices))(*devices)
+            L.check(self.lib.px_open_multi(C.byref(self.p), str(weights).encode(), devs, len(devices), nb, pptr,
+                                           pbytes), "px_open_multi")
+        else:
+            L.check(self.lib.px_open_ex(C.byref(self.p), str(weights).encode(), device, nb, pptr, pbytes),
+                    "px_open_ex")
         self.open = True
 
     @property
