@@ -262,6 +262,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
 
     if (warp == 0) {
         if (elect_one()) {

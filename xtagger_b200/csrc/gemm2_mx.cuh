@@ -99,6 +99,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     cluster_sync();  // the peer's barriers and scale factors are ready before anyone uses them
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
     const int total = g.m_tiles * g.n_tiles;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int KI = g.kiters;

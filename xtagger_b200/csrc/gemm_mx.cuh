@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(320, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
     const int total = g.m_tiles * g.n_tiles;
     const int KI = g.kiters;
 

@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
+    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
     const int total = g.n_tiles * g.t_tiles;
     const int KI = g.kiters;
 

@@ -1,5 +1,6 @@
 // Kernel launchers: pick the template instance, build the launch shape, enqueue. No allocation, no sync.
 #include <mutex>
+#include <utility>
 #include <set>
 
 #include "attention.cuh"
@@ -45,6 +46,31 @@ static int set_smem(const void *kern, size_t bytes)
     return 0;
 }
 
+// Launches of the forward's kernels with programmatic stream serialisation (programmatic dependent launch): the
+// kernel may be scheduled while the previous kernel on the stream finishes, so that its launch and on-chip set-up
+// overlap that kernel's tail; every kernel launched this way executes griddep_wait() before it touches activations.
+// Under stream capture the dependency becomes a programmatic edge of the graph. XTB_PDL=0 at build time launches
+// them plainly.
+#ifndef XTB_PDL
+#define XTB_PDL 1
+#endif
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = XTB_PDL ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // One launch of the tcgen05 GEMM: A = a (M rows), B = b (N rows), K slices of 128 bytes.
 template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
 static int run_gemm(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
@@ -75,8 +101,7 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, b.map, tmc ? *tmc : a.map, g, ep);
-    XTB_CK(cudaGetLastError());
+    XTB_CK(launch_pdl(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st, a.map, b.map, tmc ? *tmc : a.map, g, ep));
     return 0;
 }
 
@@ -112,8 +137,8 @@ static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const flo
     int pairs = max_pairs((const void *)kern, Cfg::THREADS, Cfg::SMEM);
     if (pairs <= 0) return -1;
     if (pairs > total) pairs = total;
-    kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, b.map, tmc ? *tmc : a.map, g, ep);
-    XTB_CK(cudaGetLastError());
+    XTB_CK(launch_pdl(kern, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, st, a.map, b.map, tmc ? *tmc : a.map, g,
+                      ep));
     return 0;
 }
 
@@ -178,8 +203,8 @@ static int run_gemm2_mx(const Operand &a, const Weight8 &w, int M, float ascale,
     int pairs = max_pairs((const void *)kern, Cfg::THREADS, Cfg::SMEM);
     if (pairs <= 0) return -1;
     if (pairs > total) pairs = total;
-    kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, w.op.map, w.sfmap, tmc ? *tmc : a.map, g, mx, ep);
-    XTB_CK(cudaGetLastError());
+    XTB_CK(launch_pdl(kern, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, st, a.map, w.op.map, w.sfmap,
+                      tmc ? *tmc : a.map, g, mx, ep));
     return 0;
 }
 
@@ -210,8 +235,8 @@ static int run_gemm_mx(const Operand &a, const Weight8 &w, int M, float ascale, 
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(a.map, w.op.map, tmc ? *tmc : a.map, g, mx, ep);
-    XTB_CK(cudaGetLastError());
+    XTB_CK(launch_pdl(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st, a.map, w.op.map, tmc ? *tmc : a.map, g,
+                      mx, ep));
     return 0;
 }
 
@@ -302,8 +327,7 @@ int launch_ln_e4m3(const __half *x, const float *g, const float *b, uint8_t *y, 
     int grid = LN_BLOCKS_PER_SM * num_sms(dev);
     const int need = (rows + LN_WARPS - 1) / LN_WARPS;
     if (grid > need) grid = need;
-    k_ln_e4m3<<<grid, LN_WARPS * 32, LN_SMEM, st>>>(x, g, b, y, rows, qs, error_word(dev));
-    XTB_CK(cudaGetLastError());
+    XTB_CK(launch_pdl(k_ln_e4m3, dim3(grid), dim3(LN_WARPS * 32), LN_SMEM, st, x, g, b, y, rows, qs, error_word(dev)));
     return 0;
 }
 
@@ -330,7 +354,8 @@ int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo
 {
     if (set_smem((const void *)k_attention<AttEva>, ATT_SMEM)) return -1;
     dim3 grid(AttEva::PAIRS, NH, nimg);
-    k_attention<AttEva><<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
+    XTB_CK(launch_pdl(k_attention<AttEva>, grid, dim3(ATT_THREADS), ATT_SMEM, st, a.tq, a.tk, a.tv, out, sinv, vo,
+                      error_word(current_device())));
     XTB_CK(cudaGetLastError());
     k_attention_last<<<nimg * NH, ATT_LAST_THREADS, 0, st_last ? st_last : st>>>(a.q8, a.k8, a.v8, out, sinv, vo);
     XTB_CK(cudaGetLastError());
@@ -366,7 +391,7 @@ int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __ha
 {
     CUtensorMap xm;
     if (resid_map(&xm, x, rows)) return -1;
-    k_rowstat<<<rowstat_blocks(rows), ROWSTAT_THREADS, 0, st>>>((float2 *)stat, rows);
+    XTB_CK(launch_pdl(k_rowstat, dim3(rowstat_blocks(rows)), dim3(ROWSTAT_THREADS), 0, st, (float2 *)stat, rows));
     XTB_CK(cudaGetLastError());
     return launch_fc2_gemm(h8, w, ascale, rows, xm, stat, c, d, nullptr, st);
 }
@@ -426,7 +451,8 @@ static int run_gemm_sp_k(const SparseW &w, const Operand &x, int M, float ascale
     const int total = g.n_tiles * g.t_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
-    kern<<<grid, SpCfg::THREADS, SpCfg::SMEM, st>>>(w.va, w.me, x.map, tmc ? *tmc : x.map, g, ep);
+    XTB_CK(launch_pdl(kern, dim3(grid), dim3(SpCfg::THREADS), SpCfg::SMEM, st, w.va, w.me, x.map, tmc ? *tmc : x.map, g,
+                      ep));
     XTB_CK(cudaGetLastError());
     return 0;
 }
@@ -481,7 +507,7 @@ int launch_fc2_sp(const Operand &h8, const SparseW &w, float ascale, int rows, _
 {
     CUtensorMap xm;
     if (sp_resid_map(&xm, x, rows)) return -1;
-    k_rowstat<<<rowstat_blocks(rows), ROWSTAT_THREADS, 0, st>>>((float2 *)stat, rows);
+    XTB_CK(launch_pdl(k_rowstat, dim3(rowstat_blocks(rows)), dim3(ROWSTAT_THREADS), 0, st, (float2 *)stat, rows));
     XTB_CK(cudaGetLastError());
     SpResid<true>::Params p{stat, c, d, rows};
     return run_gemm_sp<SpResid<true>>(w, h8, rows, ascale, p, st, &xm);
@@ -529,9 +555,9 @@ int launch_selftest_wait(uint32_t timeout_us, int arrive, cudaStream_t st)
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,
                    float qs_head, cudaStream_t st)
 {
-    k_pool<<<dim3(nimg, D / 64), 256, 0, st>>>(x, pool);
+    XTB_CK(launch_pdl(k_pool, dim3(nimg, D / 64), dim3(256), 0, st, x, pool));
     XTB_CK(cudaGetLastError());
-    k_ln_head<<<(nimg + 7) / 8, 256, 0, st>>>(pool, g, b, pn, pn8, nimg, qs_head);
+    XTB_CK(launch_pdl(k_ln_head, dim3((nimg + 7) / 8), dim3(256), 0, st, pool, g, b, pn, pn8, nimg, qs_head));
     XTB_CK(cudaGetLastError());
     return 0;
 }
@@ -611,7 +637,7 @@ int launch_px_patch(const Operand &in, const Operand &pe, int rows, __half *x, c
 
 int launch_px_embed(__half *x, const float *pos, const float *w, const float *b, int rows, cudaStream_t st)
 {
-    k_px_embed<<<(rows + 7) / 8, 256, 0, st>>>(x, pos, w, b, rows);
+    XTB_CK(launch_pdl(k_px_embed, dim3((rows + 7) / 8), dim3(256), 0, st, x, pos, w, b, rows));
     XTB_CK(cudaGetLastError());
     return 0;
 }
@@ -645,7 +671,8 @@ static int run_attention_seq(const Attn &a, int nseq, uint8_t *out, float sinv, 
     auto kern = k_attention<SQ>;
     if (set_smem((const void *)kern, ATT_SMEM)) return -1;
     dim3 grid(SQ::PAIRS, NH, nseq);
-    kern<<<grid, ATT_THREADS, ATT_SMEM, st>>>(a.tq, a.tk, a.tv, out, sinv, vo, error_word(current_device()));
+    XTB_CK(launch_pdl(kern, grid, dim3(ATT_THREADS), ATT_SMEM, st, a.tq, a.tk, a.tv, out, sinv, vo,
+                      error_word(current_device())));
     XTB_CK(cudaGetLastError());
     return 0;
 }
@@ -688,13 +715,13 @@ int launch_px_head(const __half *x, int nimg, const float *w, const float *b, co
     const int rows = nimg * PX_T;
     int grid = 3 * num_sms(current_device());
     if (grid > (rows + 7) / 8) grid = (rows + 7) / 8;
-    k_px_head_ln_score<<<grid, 256, PX_HEAD_SMEM, st>>>(x, w, b, hpos, U, y, s, rows);
+    XTB_CK(launch_pdl(k_px_head_ln_score, dim3(grid), dim3(256), PX_HEAD_SMEM, st, x, w, b, hpos, U, y, s, rows));
     XTB_CK(cudaGetLastError());
-    k_px_head_softmax<<<nimg * NH, 256, 0, st>>>(s, P);
+    XTB_CK(launch_pdl(k_px_head_softmax, dim3(nimg * NH), dim3(256), 0, st, s, P));
     XTB_CK(cudaGetLastError());
-    k_px_head_pool<<<dim3(nimg, PX_NCH), 512, 0, st>>>(P, y, part);
+    XTB_CK(launch_pdl(k_px_head_pool, dim3(nimg, PX_NCH), dim3(512), 0, st, P, y, part));
     XTB_CK(cudaGetLastError());
-    k_px_head_v<<<nimg * NH, 256, 0, st>>>(part, wv, o);
+    XTB_CK(launch_pdl(k_px_head_v, dim3(nimg * NH), dim3(256), 0, st, part, wv, o));
     XTB_CK(cudaGetLastError());
     return 0;
 }

@@ -290,6 +290,7 @@ __device__ __forceinline__ void px_row_stats(const float *v, float eps, float *m
 __global__ void __launch_bounds__(256) k_px_embed(__half *__restrict__ x, const float *__restrict__ pos,
                                                   const float *__restrict__ w, const float *__restrict__ b, int rows)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     __half *xr = x + (size_t)row * D;
@@ -326,6 +327,7 @@ __global__ void __launch_bounds__(256) k_px_head_ln_score(const __half *__restri
                                                           const float *__restrict__ U, __half *__restrict__ y,
                                                           float *__restrict__ s, int rows)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     extern __shared__ float sU[];
     for (int i = threadIdx.x; i < NH * D / 4; i += 256) ((float4 *)sU)[i] = __ldg((const float4 *)U + i);
     __syncthreads();
@@ -390,6 +392,7 @@ __global__ void __launch_bounds__(256) k_px_head_ln_score(const __half *__restri
 // Pool weights: P[img][h][t] = fp16(exp2(s[t][h] - max) / sum), one block per (image, head)
 __global__ void __launch_bounds__(256) k_px_head_softmax(const float *__restrict__ s, __half *__restrict__ P)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     __shared__ float red[8];
     const int img = blockIdx.x / NH, h = blockIdx.x % NH, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const float *sb = s + (size_t)img * PX_T * NH + h;
@@ -421,6 +424,7 @@ __global__ void __launch_bounds__(256) k_px_head_softmax(const float *__restrict
 __global__ void __launch_bounds__(512) k_px_head_pool(const __half *__restrict__ P, const __half *__restrict__ y,
                                                       float *__restrict__ part)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     __shared__ __align__(16) float sp[PX_PCH][NH];
     const int img = blockIdx.x, c = blockIdx.y, t0 = c * PX_PCH;
     for (int i = threadIdx.x; i < PX_PCH * NH; i += 512) {
@@ -453,6 +457,7 @@ __global__ void __launch_bounds__(512) k_px_head_pool(const __half *__restrict__
 __global__ void __launch_bounds__(256) k_px_head_v(const float *__restrict__ part, const __half *__restrict__ wv,
                                                    __half *__restrict__ o)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     __shared__ __align__(16) float xs[D];
     const int img = blockIdx.x / NH, h = blockIdx.x % NH, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const float *pv = part + ((size_t)img * PX_NCH * NH + h) * D;

@@ -23,6 +23,12 @@ enum : uint32_t {
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// Programmatic dependent launch: the kernels of the forward are launched so that they may start while the previous
+// kernel on the stream finishes. Each of them runs its on-chip set-up (barriers, TMEM, descriptor prefetch, constant
+// weights) first and then waits here until the previous kernel has completed and its memory is visible, before it
+// reads or writes any activation. Without a programmatic predecessor the wait returns at once.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t globaltimer()
 {
     uint64_t t;

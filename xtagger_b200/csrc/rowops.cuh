@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32, LN_BLOCKS_PER_SM)
     uint64_t *bar = (uint64_t *)(ln_smem + LN_WARPS * LN_DEPTH * D * 2) + wl * LN_DEPTH;
     const int W = gridDim.x * LN_WARPS;
     const int w0 = blockIdx.x * LN_WARPS + wl;
+    griddep_wait();  // the previous kernel of the stream has completed: x may be read, y written
     if (lane == 0) {
         for (int s = 0; s < LN_DEPTH; s++) mbar_init(&bar[s], 1);
         fence_mbar_init();
@@ -134,6 +135,7 @@ __global__ void k_selftest_wait(uint64_t ns, int arrive, uint32_t *err)
 // batches still spread the partial loads over the SMs.
 __global__ void __launch_bounds__(ROWSTAT_THREADS) k_rowstat(float2 *__restrict__ stat, int rows)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     const int t = blockIdx.x * ROWSTAT_THREADS + threadIdx.x, row = t >> 2;
     const float2 ms = rowstat_of(stat, rows, row, t & 3);
     __syncwarp();  // every part has read partial 0 of its row before part 0 overwrites it
@@ -145,6 +147,7 @@ __global__ void __launch_bounds__(ROWSTAT_THREADS) k_rowstat(float2 *__restrict_
 // partials are added in a fixed order. Replaces k_pool (eva_kernels.cu:404-431).
 __global__ void __launch_bounds__(256) k_pool(const __half *__restrict__ x, float *__restrict__ pool)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     __shared__ float4 red[16][16];
     const int c = threadIdx.x & 15, grp = threadIdx.x >> 4;
     const __half *xr = x + ((size_t)blockIdx.x * T + 1 + grp * 64) * D + blockIdx.y * 64 + 4 * c;
@@ -179,6 +182,7 @@ __global__ void __launch_bounds__(256) k_ln_head(const float *__restrict__ pool,
                                                  const float *__restrict__ bta, __half *__restrict__ pn,
                                                  uint8_t *__restrict__ pn8, int nimg, float qs)
 {
+    griddep_wait();  // the previous kernel of the stream has completed
     const int img = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (img >= nimg) return;
     const float4 *xr = (const float4 *)(pool + (size_t)img * D);
