@@ -446,15 +446,27 @@ __global__ void __launch_bounds__(ATT_LAST_THREADS)
         for (int x = 0; x < 4; x++) sq[4 * tid + x] = f[x];
     }
     __syncthreads();
-    // scores: keys tid, tid + 256, ...; four partial sums per dot product
-    for (int key = tid; key < ATT_NSUB * 64; key += ATT_LAST_THREADS) {
+    // scores: keys tid, tid + 256, ...; four partial sums per dot product. Every key row of the thread is loaded
+    // before any is used, so the loads' latencies overlap instead of adding up.
+    constexpr int KPT_LAST = (ATT_NSUB * 64 + ATT_LAST_THREADS - 1) / ATT_LAST_THREADS;
+    uint4 krow[KPT_LAST][4];
+#pragma unroll
+    for (int j = 0; j < KPT_LAST; j++) {
+        const int key = tid + j * ATT_LAST_THREADS;
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            krow[j][c] = key < T ? __ldg((const uint4 *)(k8 + (base + key) * 64) + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < KPT_LAST; j++) {
+        const int key = tid + j * ATT_LAST_THREADS;
+        if (key >= ATT_NSUB * 64) break;
         float sc = -INFINITY;
         if (key < T) {
-            const uint4 *kr = (const uint4 *)(k8 + (base + key) * 64);
             float a4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                const uint4 w = __ldg(kr + c);
+                const uint4 w = krow[j][c];
                 const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
@@ -519,12 +531,19 @@ __global__ void __launch_bounds__(ATT_LAST_THREADS)
         const int dp = tid & 31, qk = tid >> 5;   // dims 2 dp, 2 dp + 1; keys of quarter qk % 4 in tiles (qk / 4) ...
         float o0 = 0.f, o1 = 0.f;
         for (int u = qk >> 2; u < ATT_NSUB; u += 2) {
-            const int k0 = u * 64 + (qk & 3) * 16, k1 = min(k0 + 16, T);
+            const int k0 = u * 64 + (qk & 3) * 16;
+            // the run's 16 value pairs first (keys past the sequence read as zero and are skipped below), then the
+            // products in key order
+            uint32_t vv[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                vv[i] = k0 + i < T ? __ldg((const unsigned short *)(v8 + (base + k0 + i) * 64) + dp) : 0u;
             float a0 = 0.f, a1 = 0.f;
-            for (int key = k0; key < k1; key++) {
-                const float pq = ss[key];
-                const uint32_t vv = __ldg((const unsigned short *)(v8 + (base + key) * 64) + dp);
-                const float2 vf = __half22float2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)vv, __NV_E4M3));
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                if (k0 + i >= T) break;
+                const float pq = ss[k0 + i];
+                const float2 vf = __half22float2(__nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)vv[i], __NV_E4M3));
                 a0 = fmaf(pq, vf.x, a0);
                 a1 = fmaf(pq, vf.y, a1);
             }
