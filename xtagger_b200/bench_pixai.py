@@ -7,9 +7,8 @@ pixai.bin v3 weights (E4M3, one scale per tensor), seeded synthetic 1008^2 image
   roofline     fc1 (the largest GEMM): dense FP8 FLOPs per launch over its time in one direct forward with events
                after every kernel, against 2x the measured bf16 sustained peak;
   profile_ms   per-kind kernel times of that forward;
-  cpu          with --cpu: the CPU oracle (plain C + OpenMP) on one image, full model.
 
-    python -m xtagger_b200.bench_pixai [--batch 8] [--steps 10] [--warmup 3] [--cpu]
+    python -m xtagger_b200.bench_pixai [--batch 8] [--steps 10] [--warmup 3]
 """
 import argparse
 import json
@@ -41,7 +40,6 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--nt", type=int, default=30877)
-    ap.add_argument("--cpu", action="store_true", help="also time the CPU oracle on one image (about a minute)")
     a = ap.parse_args()
     import sys
     sys.path.insert(0, ROOT)
@@ -97,14 +95,6 @@ def main():
                          "achieved": achieved, "peak": pk, "unit": "TFLOP/s", "frac": achieved / pk,
                          "peak_source": src, "launch_ms": fc1_ms},
             "profile_ms": prof, "gpu_launches_per_forward": launches, "clocks": clocks}
-    if a.cpu:
-        from oracle import oracle as O
-        x = pool[:1]
-        t0 = time.perf_counter()
-        O.px_forward(model, x)
-        dt = time.perf_counter() - t0
-        line["cpu"] = {"value": 1 / dt, "unit": "images/s", "cores": O.lib().or_threads(), "kind": "port",
-                       "sample": f"1 image, full 32-block forward ({dt:.1f} s), CPU oracle (plain C + OpenMP)"}
     print(json.dumps(line), flush=True)
 
 

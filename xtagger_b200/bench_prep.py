@@ -3,10 +3,8 @@ seeded synthetic images, through the C ABI. Per workload (image size, alpha) one
   device_img_s   images/s with the decoded images resident in HBM (a CUDA graph of `batch` images, CUDA events);
   e2e_img_s      the same including the copy of each decoded image from pinned host memory (H2D on the stream);
   gbs            decoded-image bytes read per second (device-resident);
-  cpu            the CPU oracle (plain C, one thread) on one image of the same size;
   level          the pyramid level the whole-image resample reads from.
-The reference does this step on the host (src/core/procimg.h, AVX2 per worker thread); its numbers are not
-reproducible here (Windows-only build), so the oracle port stands in as the CPU baseline.
+The reference does this step on the host (src/core/procimg.h, AVX2 per worker thread).
 
     python -m xtagger_b200.bench_prep [--batch 64] [--iters 10] [--sizes 0,1,2,3]
 """
@@ -15,12 +13,23 @@ import ctypes as C
 import json
 import os
 import sys
-import time
 
 import numpy as np
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 WORKLOADS = [(1024, 1024, 1), (1600, 1200, 0), (3000, 2000, 1), (448, 448, 0)]
+
+
+def _level(w, h, S=448):
+    """Pyramid level a whole-image resample reads from: halve while the next level's long side stays >= 2 S, then the
+    coarsest level that still leaves a factor >= 2 (procimg.h:665-697)."""
+    lw, lh, nlv = w, h, 1
+    while nlv < 12 and (max(lw, lh) >> 1) >= 2 * S and lw >= 2 and lh >= 2:
+        lw, lh, nlv = lw >> 1, lh >> 1, nlv + 1
+    side, L = max(w, h), 0
+    while L + 1 < nlv and (side >> (L + 1)) >= 2 * S:
+        L += 1
+    return L
 
 
 def main():
@@ -31,7 +40,6 @@ def main():
     a = ap.parse_args()
     sys.path.insert(0, ROOT)
     import torch
-    from oracle import oracle as O
     from xtagger_b200 import lib as L
     xl = L.lib()
     rng = np.random.default_rng(5)
@@ -76,18 +84,12 @@ def main():
             res[copy] = float(np.median(ts))
             del g
         assert xl.xtb_error_word(0) == 0
-        img = host[0].numpy().copy()
-        o = np.zeros(1024 * 592, np.uint16)
-        t0 = time.perf_counter()
-        O.lib().or_prep(img, w, h, stride, alpha, 0, 0, w, h, o)
-        cpu = time.perf_counter() - t0
         print(json.dumps({"workload": f"{w}x{h} RGBA{' with alpha' if alpha else ''}, whole image -> 448^2 input",
-                          "batch": a.batch, "level": O.lib().or_prep_level(w, h, max(w, h)),
+                          "batch": a.batch, "level": _level(w, h),
                           "device_img_s": a.batch / res[False], "e2e_img_s": a.batch / res[True],
                           "us_per_img": res[False] / a.batch * 1e6,
                           "gbs": a.batch * h * stride / res[False] / 1e9,
-                          "h2d_bytes_per_img": h * stride,
-                          "cpu": {"img_s": 1 / cpu, "cores": 1, "kind": "port"}}), flush=True)
+                          "h2d_bytes_per_img": h * stride}), flush=True)
 
 
 if __name__ == "__main__":
