@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 {
     constexpr int NSUB = SQ::NSUB, NK = SQ::NK, RS = SQ::RS, L = SQ::L;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sQ = smem;                                  // [ATT_G]
     uint8_t *sK = sQ + ATT_G * ATT_Q_BYTES;              // [ATT_KS]
     uint8_t *sV = sK + ATT_KS * ATT_K_BYTES;             // [ATT_KS]

@@ -72,6 +72,19 @@ struct StreamOf<E, decltype((void)E::STREAM)> {
     static constexpr bool v = E::STREAM;
 };
 
+// Epilogues with apply_last(params, acc[COLS], ctx, state, wide) (Epi::LAST_WIDE): on a CTA's last tile the
+// operand ring is idle once the final accumulator is ready, and each epilogue warp gets 32 x COLS x 4 bytes of it
+// (`wide`) to stage its whole slice at once. The accumulator registers are then free for the stores, which no
+// longer run one latency-bound iteration at a time.
+template <class E, class = void>
+struct LastWideOf {
+    static constexpr bool v = false;
+};
+template <class E>
+struct LastWideOf<E, decltype((void)E::LAST_WIDE)> {
+    static constexpr bool v = E::LAST_WIDE;
+};
+
 // Epilogue context of one thread: output row row0 + lane, columns col0 .. col0 + COLS - 1.
 struct EpiCtx {
     int row0;        // first row of this warp's 32 rows
@@ -116,7 +129,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     constexpr int COLS = C::COLS;
     constexpr uint32_t IDESC = idesc_m128(BN);
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * C::A_BYTES;
     uint8_t *sStage = smem + STAGES * C::STAGE_BYTES;
@@ -292,6 +305,13 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
                 }
             }
             if (!ok) break;
+            if constexpr (LastWideOf<Epi>::v) {
+                static_assert((size_t)STAGES * C::STAGE_BYTES >= (size_t)EW * 32 * COLS * 4, "ring too small to stage");
+                if (t + (int)gridDim.x >= total) {  // last tile: every MMA has read its operands, no load follows
+                    Epi::apply_last(ep, (float *)acc, cx, es, smem + (size_t)ew * 32 * COLS * 4);
+                    continue;
+                }
+            }
             Epi::apply(ep, (float *)acc, cx, es);
         }
         if (lane == 0) bulk_wait0();  // the epilogue's TMA stores / reductions have completed
@@ -320,24 +340,87 @@ struct EpiF32 {
     using State = NoState;
     __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
     __device__ __forceinline__ static void begin(const Params &, const EpiCtx &, State &) {}
+    // Each 32 x 32 chunk goes out through the staging buffer, a warp store covering two rows (half a warp per row,
+    // two columns per lane): with an even row stride and an 8-byte aligned output (the usual case: N = 2730 gives
+    // 10,920-byte rows, 8- but not 16-byte aligned) one float2 store per lane, half as many store instructions as
+    // one float per lane; otherwise two float stores.
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &)
     {
+        const bool pairs = (p.ld & 1) == 0 && ((uintptr_t)p.out & 7) == 0;
+        const int rr = cx.lane >> 4, cc = (cx.lane & 15) * 2;
 #pragma unroll
         for (int c = 0; c < COLS / 32; c++) {
             __syncwarp();
             stage_row_f32(cx.stage, cx.lane, acc + 32 * c);
             __syncwarp();
-            // every staged value into registers first, then the stores back to back: a staging load issued after a
-            // global store through a pointer the compiler cannot tell apart from it is ordered behind that store,
-            // which made the warp wait out each store's latency in turn
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = stage_f32(cx.stage, i, cx.lane);
-            const int col = cx.col0 + 32 * c + cx.lane;
+            const int col = cx.col0 + 32 * c + cc;
             if (col < p.N) {
+#pragma unroll 4
+                for (int i = 0; i < 16; i++) {
+                    const int row = cx.row0 + 2 * i + rr;
+                    if (row < p.M) {
+                        const float2 v = stage_f32x2(cx.stage, 2 * i + rr, cc);
+                        float *o = p.out + (size_t)row * p.ld + col;
+                        if (pairs && col + 1 < p.N) {
+                            *(float2 *)o = v;
+                        } else {
+                            o[0] = v.x;
+                            if (col + 1 < p.N) o[1] = v.y;
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+
+    // Last tile: the warp's 32 x COLS slice goes to `wide` (row r at r * COLS * 4 bytes, its 16-byte chunks
+    // XOR-swizzled by r & 7: conflict-free both for one row per lane and for whole rows across the warp), then out
+    // with 32 / (COLS / 4) rows per warp instruction, four columns per lane: a float4 where the row's first column is
+    // 16-byte aligned, else two float2 or, for an odd row stride or an unaligned output, floats. Eight instructions'
+    // loads are in flight before their stores.
+    static constexpr bool LAST_WIDE = true;
+    __device__ __forceinline__ static uint8_t *wide_chunk(uint8_t *w, int r, int c)
+    {
+        return w + r * (COLS * 4) + (((c ^ (r & 7)) & (COLS / 4 - 1)) << 4);
+    }
+    __device__ __forceinline__ static void apply_last(const Params &p, const float *acc, const EpiCtx &cx, State &,
+                                                      uint8_t *wide)
+    {
+        static_assert(COLS == 64 || COLS == 128, "a warp instruction covers one or two whole rows");
+        constexpr int LPR = COLS / 4;   // lanes per row
+        constexpr int RPI = 32 / LPR;   // rows per instruction
+        __syncwarp();
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (cx.row0 + i < p.M) p.out[(size_t)(cx.row0 + i) * p.ld + col] = v[i];
+        for (int c = 0; c < COLS / 4; c++)
+            *(float4 *)wide_chunk(wide, cx.lane, c) = make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+        __syncwarp();
+        const int sub = cx.lane / LPR, ch = cx.lane % LPR;
+        const int col = cx.col0 + 4 * ch;
+        const bool al8 = (p.ld & 1) == 0 && ((uintptr_t)p.out & 7) == 0;
+        const bool out16 = ((uintptr_t)p.out & 15) == 0;
+#pragma unroll 1
+        for (int i0 = 0; i0 < 32; i0 += 8 * RPI) {
+            float4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = *(const float4 *)wide_chunk(wide, i0 + i * RPI + sub, ch);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int row = cx.row0 + i0 + i * RPI + sub;
+                if (row >= p.M || col >= p.N) continue;
+                float *o = p.out + (size_t)row * p.ld + col;
+                const uint32_t e = (uint32_t)row * (uint32_t)p.ld + (uint32_t)cx.col0;  // low bits of the row's first element offset
+                if (col + 3 < p.N && out16 && (e & 3) == 0) {
+                    *(float4 *)o = v[i];
+                } else if (col + 3 < p.N && al8) {
+                    *(float2 *)o = make_float2(v[i].x, v[i].y);
+                    *(float2 *)(o + 2) = make_float2(v[i].z, v[i].w);
+                } else {
+                    o[0] = v[i].x;
+                    if (col + 1 < p.N) o[1] = v[i].y;
+                    if (col + 2 < p.N) o[2] = v[i].z;
+                    if (col + 3 < p.N) o[3] = v[i].w;
+                }
             }
         }
         __syncwarp();

@@ -61,7 +61,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN, GROUPS
     constexpr int STAGES = C::STAGES, TBUF = C::TBUF, COLS = C::COLS;
     constexpr uint32_t IDESC = idesc_m256(C::BN);
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * C::A_BYTES;
     uint8_t *sStage = smem + STAGES * C::STAGE_BYTES;

@@ -59,7 +59,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     using C = Gemm2MxCfg<StagingOf<Epi>::v, NB2>;
     constexpr int STAGES = C::STAGES, COLS = C::COLS;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sA = smem;
     uint8_t *sB = sA + STAGES * C::A_BYTES;
     uint8_t *sSF = sB + STAGES * C::B_BYTES;            // [STAGES][512]

@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(SpCfg::THREADS, 1)
     constexpr int STAGES = C::STAGES;
     constexpr uint32_t IDESC = idesc_sp_m128(SP_BT);
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sA = smem;                       // weight values: 64B-swizzle atoms (512 bytes) need 512-byte alignment
     uint8_t *sB = sA + STAGES * C::A_BYTES;   // activations: 128B swizzle, 1024-byte aligned (14 KB per stage)
     uint8_t *sE = sB + STAGES * C::B_BYTES;   // metadata

@@ -51,6 +51,11 @@ static int set_smem(const void *kern, size_t bytes)
 // overlap that kernel's tail; every kernel launched this way executes griddep_wait() before it touches activations.
 // Under stream capture the dependency becomes a programmatic edge of the graph. XTB_PDL=0 at build time launches
 // them plainly.
+// XTB_BALANCED_GRID=1 at build time: the single-CTA GEMM spreads its tiles evenly (fewer CTAs, the same number of
+// tiles on the busiest one) instead of one CTA per SM.
+#ifndef XTB_BALANCED_GRID
+#define XTB_BALANCED_GRID 0
+#endif
 #ifndef XTB_PDL
 #define XTB_PDL 1
 #endif
@@ -101,6 +106,10 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
+#if XTB_BALANCED_GRID
+    const int per = (total + grid - 1) / grid;  // tiles of the busiest CTA: spread them evenly over fewer CTAs
+    grid = (total + per - 1) / per;
+#endif
     XTB_CK(launch_pdl(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st, a.map, b.map, tmc ? *tmc : a.map, g, ep));
     return 0;
 }
@@ -256,7 +265,15 @@ static constexpr bool kPair[5] = {(XTB_PAIR_MASK & 1) != 0 && !kPairG[0], (XTB_P
                                   (XTB_PAIR_MASK & 4) != 0 && !kPairG[2], (XTB_PAIR_MASK & 8) != 0 && !kPairG[3],
                                   (XTB_PAIR_MASK & 16) != 0 && !kPairG[4]};
 
-int weight_box_rows(WeightUse u) { return kPairG[u] ? Gemm2GCfg::BN / 2 : kPair[u] ? Gemm2Cfg::BN / 2 : 256; }
+// Tile width of the single-CTA GEMM per weight use: 256 for the forward's projections; the stand-alone fp32-output
+// GEMM (W_F32) takes XTB_F32_BN.
+#ifndef XTB_F32_BN
+#define XTB_F32_BN 256
+#endif
+static constexpr int kSingleBN[5] = {256, 256, 256, 256, XTB_F32_BN};
+using EpiF32Out = EpiF32<XTB_F32_BN / 2>;
+
+int weight_box_rows(WeightUse u) { return kPairG[u] ? Gemm2GCfg::BN / 2 : kPair[u] ? Gemm2Cfg::BN / 2 : kSingleBN[u]; }
 
 template <class Epi, WeightUse U>
 static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, const typename Epi::Params &ep, cudaStream_t st,
@@ -270,15 +287,16 @@ static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, con
         if constexpr (kPair[U])
             return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
         else
-            return run_gemm<Epi, 256, false, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err,
-                                                           w.uniform);
+            return run_gemm<Epi, kSingleBN[U], false, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc,
+                                                                    err, w.uniform);
     }
     if constexpr (kPairG[U])
         return run_gemm2<Epi, 128, true>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else if constexpr (kPair[U])
         return run_gemm2<Epi>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else
-        return run_gemm<Epi, 256, false, true, false>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
+        return run_gemm<Epi, kSingleBN[U], false, true, false>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st,
+                                                               tmc, err);
 }
 
 // Opt the projection kernel of (Epi, U) into its shared memory and check that its clusters fit (pair kernels).
@@ -297,8 +315,8 @@ static int prepare_proj()
                    ? -1
                    : 0;
     } else {
-        return set_smem((const void *)k_gemm<Epi, 256, false, true, false>, GemmCfg<256>::SMEM) ||
-                       set_smem((const void *)k_gemm<Epi, 256, false, false, false>, GemmCfg<256>::SMEM)
+        return set_smem((const void *)k_gemm<Epi, kSingleBN[U], false, true, false>, GemmCfg<kSingleBN[U]>::SMEM) ||
+                       set_smem((const void *)k_gemm<Epi, kSingleBN[U], false, false, false>, GemmCfg<kSingleBN[U]>::SMEM)
                    ? -1
                    : 0;
     }
@@ -306,8 +324,8 @@ static int prepare_proj()
 
 int launch_gemm_f32(const Operand &a, const Weight8 &w, float ascale, float *out, int ldo, cudaStream_t st)
 {
-    EpiF32<128>::Params p{out, ldo, a.rows, w.n};
-    return run_proj<EpiF32<128>, W_F32>(a, w, a.rows, ascale, p, st);
+    EpiF32Out::Params p{out, ldo, a.rows, w.n};
+    return run_proj<EpiF32Out, W_F32>(a, w, a.rows, ascale, p, st);
 }
 
 int launch_patch_embed(const Operand &in, const Operand &pe, int nimg, const float *pos, __half *x, cudaStream_t st)
@@ -588,7 +606,7 @@ int prepare_kernels()
     for (const void *k : single)
         if (set_smem(k, GemmCfg<256>::SMEM)) return -1;
     if (prepare_proj<EpiQKV, W_QKV>() || prepare_proj<EpiResid, W_O>() || prepare_proj<EpiFC1, W_FC1>() ||
-        prepare_proj<EpiFC2, W_FC2>() || prepare_proj<EpiF32<128>, W_F32>())
+        prepare_proj<EpiFC2, W_FC2>() || prepare_proj<EpiF32Out, W_F32>())
         return -1;
     const void *g64[] = {(const void *)k_gemm<EpiHead<32>, 64, true, false, false>,
                          (const void *)k_gemm<EpiHead<32>, 64, false, true, true>};

@@ -22,6 +22,10 @@ enum : uint32_t {
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// The dynamic shared memory block rounded up to 1024 bytes (128B-swizzled TMA tiles and UMMA descriptors want it).
+// Pointer arithmetic on the __shared__ array itself, not an integer round trip: the compiler can then still tell that
+// every pointer derived from the result is shared memory and address it as such rather than generically.
+__device__ __forceinline__ uint8_t *smem_align1024(uint8_t *raw) { return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u); }
 
 // Programmatic dependent launch: the kernels of the forward are launched so that they may start while the previous
 // kernel on the stream finishes. Each of them runs its on-chip set-up (barriers, TMEM, descriptor prefetch, constant
