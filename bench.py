@@ -210,6 +210,14 @@ def run_reference(args, rank, world):
                              "sample": "1 image per step, full 24-layer forward, CPU restatement (oracle/) of the "
                                        "reference's GPU forward; the reference ships no CPU path"},
             "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_extra:
+        # The reference's own GPU kernels (compiled from its sources into oracle/_ref) on GPU 0 of this box, at the
+        # same batch: its eva_forward replayed as a CUDA graph with the inputs resident, on its v3 weight format.
+        try:
+            from oracle import ref_time as RT
+            line["reference_gpu_kernels"] = RT.reference_kernels([args.batch], warmup=3, iters=10, nt=args.nt)[0]
+        except Exception as e:  # no GPU, or the reference library not built here
+            line["reference_gpu_kernels"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(line), flush=True)
 
 

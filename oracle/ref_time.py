@@ -32,21 +32,38 @@ def main():
     if a.pixai:
         return pixai(a)
     a.nt = a.nt or 10861
+    for line in reference_kernels(a.batch, a.warmup, a.iters, a.nt):
+        print(json.dumps(line), flush=True)
+
+
+def reference_kernels(batches, warmup=3, iters=10, nt=10861):
+    """One dict per batch size: the reference's eva_forward replayed as a CUDA graph on GPU 0 (inputs resident)."""
+    import torch
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device")
     from xtagger_b200 import model as M
-    lib = C.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so"))
+    so = os.path.join(ROOT, "oracle", "_ref", "libref_kernels.so")
+    if not os.path.exists(so):
+        raise FileNotFoundError(so + " not built (oracle/Makefile ref, where the reference sources are present)")
+    lib = C.CDLL(so)
     lib.ref_forward_time.restype = C.c_int
     lib.ref_forward_time.argtypes = [C.c_char_p, np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS"), C.c_int,
                                      C.c_int, C.c_int, C.POINTER(C.c_float)]
-    path = M.write_synthetic(os.path.join(tempfile.mkdtemp(), "v3.bin"), seed=0, nt=a.nt, nl=24, version=3,
+    path = M.write_synthetic(os.path.join(tempfile.mkdtemp(), "v3.bin"), seed=0, nt=nt, nl=24, version=3,
                              head_fp8=False)
-    for nb in a.batch:
-        x = np.ascontiguousarray(M.synthetic_inputs(nb, seed=1))
-        ms = C.c_float(0)
-        if lib.ref_forward_time(path.encode(), x, nb, a.warmup, a.iters, C.byref(ms)):
-            raise SystemExit("reference forward failed")
-        print(json.dumps({"impl": "reference kernels (eva_kernels.cu, mma.sync E4M3) on this GPU", "batch": nb,
-                          "ms_per_forward": ms.value, "images_per_s": nb / (ms.value * 1e-3),
-                          "model": f"v3, 24 layers, fp16 head, {a.nt} tags, random-init"}), flush=True)
+    out = []
+    try:
+        for nb in batches:
+            x = np.ascontiguousarray(M.synthetic_inputs(nb, seed=1))
+            ms = C.c_float(0)
+            if lib.ref_forward_time(path.encode(), x, nb, warmup, iters, C.byref(ms)):
+                raise RuntimeError("reference forward failed")
+            out.append({"impl": "reference kernels (eva_kernels.cu, mma.sync E4M3) on this GPU", "batch": nb,
+                        "ms_per_forward": ms.value, "images_per_s": nb / (ms.value * 1e-3),
+                        "model": f"v3, 24 layers, fp16 head, {nt} tags, random-init"})
+    finally:
+        os.remove(path)
+    return out
 
 
 def pixai(a):

@@ -29,6 +29,7 @@ def test_reference_arm_line(tmp_path):
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert "no CUDA device" in d["reference_gpu_kernels"]["unavailable"]  # the reference's GPU kernels need a GPU
 
 
 def test_reference_arm_other_ranks_exit_quietly(tmp_path):

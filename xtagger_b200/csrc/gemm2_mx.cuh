@@ -50,6 +50,11 @@ struct Gemm2MxCfg {
     static_assert(STAGES >= 4 && SMEM <= 232448, "shared memory budget");
 };
 
+// XTB_PREFETCH_W=0 at build time: no weight loads before the grid-dependency wait.
+#ifndef XTB_PREFETCH_W
+#define XTB_PREFETCH_W 1
+#endif
+
 template <class Epi, int NB2 = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     k_gemm2_mx(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -99,29 +104,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     cluster_sync();  // the peer's barriers and scale factors are ready before anyone uses them
     tc_fence_after();
     const uint32_t tbase = *tslot;
-    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
     const int total = g.m_tiles * g.n_tiles;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int KI = g.kiters;
+    if (warp != 0) griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
 
     if (warp == 0) {
         if (elect_one()) {
             const uint32_t full0 = mapa_shared(smem_u32(full), 0);
+            // Weights (B rows and scale records) are not written by earlier kernels: the first tile's first ring
+            // slots get theirs before the wait, so that their load latency overlaps the previous kernel's tail.
+            // These slots are in their first round (no consumer to wait for); the expected bytes include A's.
+            const int pre = (XTB_PREFETCH_W && pair < total) ? min(STAGES, KI) : 0;
+            for (int k = 0; k < pre; k++) {
+                const int nb = pair % g.n_tiles;
+                const uint32_t fb = full0 + k * 8;
+                mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES + C::SF_BYTES);
+#pragma unroll
+                for (int j = 0; j < NB2; j++) {
+                    const int wb = nb * NB2 + j;
+                    tma_load_2d_pair(sB + k * C::B_BYTES + j * 8192, &tmB, fb, k * 128, wb * 128 + rank * 64);
+                    tma_load_2d_pair(sSF + k * C::SF_BYTES + j * 512, &tmSF, fb, 0, 2 * (k * mx.nbp + wb));
+                }
+            }
+            griddep_wait();
             int stage = 0;
             uint32_t ph = 0;
             bool ok = true;
             for (int t = pair; t < total && ok; t += npairs) {
                 const int nb = t % g.n_tiles, mb = t / g.n_tiles;
                 for (int k = 0; k < KI; k++) {
-                    if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                    const bool early = t == pair && k < pre;  // B and scales already on their way
                     const uint32_t fb = full0 + stage * 8;
-                    mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES + C::SF_BYTES);
+                    if (!early) {
+                        if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                        mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES + C::SF_BYTES);
+                    }
                     tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, fb, k * 128, mb * 256 + rank * 128);
+                    if (!early) {
 #pragma unroll
-                    for (int j = 0; j < NB2; j++) {  // weight block nb NB2 + j: B rows and its scale record
-                        const int wb = nb * NB2 + j;
-                        tma_load_2d_pair(sB + stage * C::B_BYTES + j * 8192, &tmB, fb, k * 128, wb * 128 + rank * 64);
-                        tma_load_2d_pair(sSF + stage * C::SF_BYTES + j * 512, &tmSF, fb, 0, 2 * (k * mx.nbp + wb));
+                        for (int j = 0; j < NB2; j++) {  // weight block nb NB2 + j: B rows and its scale record
+                            const int wb = nb * NB2 + j;
+                            tma_load_2d_pair(sB + stage * C::B_BYTES + j * 8192, &tmB, fb, k * 128, wb * 128 + rank * 64);
+                            tma_load_2d_pair(sSF + stage * C::SF_BYTES + j * 512, &tmSF, fb, 0, 2 * (k * mx.nbp + wb));
+                        }
                     }
                     if (++stage == STAGES) {
                         stage = 0;

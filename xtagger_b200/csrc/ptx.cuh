@@ -31,7 +31,20 @@ __device__ __forceinline__ uint8_t *smem_align1024(uint8_t *raw) { return raw + 
 // kernel on the stream finishes. Each of them runs its on-chip set-up (barriers, TMEM, descriptor prefetch, constant
 // weights) first and then waits here until the previous kernel has completed and its memory is visible, before it
 // reads or writes any activation. Without a programmatic predecessor the wait returns at once.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Once past the wait, the kernel lets the next one launch (griddepcontrol.launch_dependents): that kernel's CTAs are
+// placed as SMs free up and run their own set-up, then block in their wait until this kernel has completed. A kernel
+// triggers only after its own wait, so at most one kernel ahead is in its set-up; and the trigger takes effect only
+// when every CTA of this grid has issued it, so CTAs that wait never keep this grid's CTAs from being placed.
+#ifndef XTB_PDL_TRIGGER
+#define XTB_PDL_TRIGGER 1
+#endif
+__device__ __forceinline__ void griddep_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#if XTB_PDL_TRIGGER
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
 
 __device__ __forceinline__ uint64_t globaltimer()
 {

@@ -25,10 +25,21 @@ __global__ void __launch_bounds__(LN_WARPS * 32, LN_BLOCKS_PER_SM)
     uint64_t *bar = (uint64_t *)(ln_smem + LN_WARPS * LN_DEPTH * D * 2) + wl * LN_DEPTH;
     const int W = gridDim.x * LN_WARPS;
     const int w0 = blockIdx.x * LN_WARPS + wl;
-    griddep_wait();  // the previous kernel of the stream has completed: x may be read, y written
     if (lane == 0) {
         for (int s = 0; s < LN_DEPTH; s++) mbar_init(&bar[s], 1);
         fence_mbar_init();
+    }
+    float gv[32], bv[32];  // gamma / beta are weights: loaded before the wait
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int c = 8 * (lane + 32 * i);
+        *(float4 *)(gv + 8 * i) = __ldg((const float4 *)(g + c));
+        *(float4 *)(gv + 8 * i + 4) = __ldg((const float4 *)(g + c + 4));
+        *(float4 *)(bv + 8 * i) = __ldg((const float4 *)(bta + c));
+        *(float4 *)(bv + 8 * i + 4) = __ldg((const float4 *)(bta + c + 4));
+    }
+    griddep_wait();  // the previous kernel of the stream has completed: x may be read, y written
+    if (lane == 0) {
         for (int s = 0; s < LN_DEPTH; s++) {
             const int r = w0 + s * W;
             if (r < rows) {
@@ -38,15 +49,6 @@ __global__ void __launch_bounds__(LN_WARPS * 32, LN_BLOCKS_PER_SM)
         }
     }
     __syncwarp();
-    float gv[32], bv[32];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int c = 8 * (lane + 32 * i);
-        *(float4 *)(gv + 8 * i) = __ldg((const float4 *)(g + c));
-        *(float4 *)(gv + 8 * i + 4) = __ldg((const float4 *)(g + c + 4));
-        *(float4 *)(bv + 8 * i) = __ldg((const float4 *)(bta + c));
-        *(float4 *)(bv + 8 * i + 4) = __ldg((const float4 *)(bta + c + 4));
-    }
     for (int k = 0, row = w0; row < rows; k++, row += W) {
         const int s = k % LN_DEPTH;
         if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (k / LN_DEPTH) & 1, err, XTB_ERR_WAIT_TMA))) return;
