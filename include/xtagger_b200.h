@@ -139,7 +139,7 @@ int xtb_oproj(const uint8_t *a, int rows, const uint8_t *w, const float *ws, flo
 int xtb_fc1(const uint8_t *h, int rows, const uint8_t *w, const float *ws, float ascale, uint8_t *h8, float *stat,
             const float *rs, void *stream);
 /* fc2 with the MLP LayerNorm folded in: x += rstd (acc - mean c) + d. Replaces k_fc2 (eva_kernels.cu:286-334).
- * stat: fc1's partials [43][rows][2]; consumed: each row's (mean, rstd) is written into partial 0. */
+ * stat: fc1's partials [43][rows][2], only read: the GEMM's epilogue sums each row's partials itself. */
 int xtb_fc2(const uint8_t *h8, int rows, const uint8_t *w, const float *ws, float ascale, uint16_t *x, float *stat,
             const float *c, const float *d, void *stream);
 /* Patch embedding (fp16 tcgen05 GEMM) + position rows: in [img][1024][592] fp16 -> x [img][1025][1024] fp16.

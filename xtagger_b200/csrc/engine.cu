@@ -2,7 +2,7 @@
 //
 // Bring-up (eva_open / eva_open_ex -> boot thread): read the weight file (v3 per-tensor or v4 block-scaled) into
 // pinned host memory, copy it to every device, resolve the tensor layout, allocate the activations for the
-// device's batch, build the TMA descriptors, capture the whole forward (220 launches) into one CUDA graph per
+// device's batch, build the TMA descriptors, capture the whole forward (196 launches) into one CUDA graph per
 // device (one per input buffer). Per batch (eva_submit): H2D of the inputs (adjacent pool inputs in one copy) on a
 // copy stream into one of two input buffers, graph launch once they have landed, D2H of the
 // scores (and head inputs), event; eva_wait sleeps on the events. Multi-GPU: one replica per device with its own
@@ -318,7 +318,7 @@ int forward(Impl *im, Replica &r, eva *e, Prof *p)
         if (sm & 8) RCK(launch_fc2_sp(r.op_h8_sp, L.sw[3], L.adq[3], rows, r.x, r.stat, L.c, L.d, st));
         else RCK(launch_fc2(r.op_h8, L.w[3], L.adq[3], rows, r.x, r.stat, L.c, L.d, st));
         RCK(record(p, st, P_FC2));
-        n += 9;  // ln1, qkv, attention (2), oproj, ln2, fc1, fc2 (row statistics + GEMM)
+        n += (sm & 8) ? 9 : 8;  // ln1, qkv, attention (2), oproj, ln2, fc1, fc2 (+ row statistics when sparse)
     }
     RCK(launch_pool_ln(r.x, nb, r.fnw, r.fnb, r.pool, r.pn, im->head8 ? r.pn8 : nullptr, 1.0f / im->head_adq, st));
     n += 2;

@@ -21,6 +21,13 @@ namespace xtb {
 // per row (lanes 4 i .. 4 i + 3 of a warp: `row`, part j = lane & 3): part j adds partials j, j + 4, ... in order, and
 // the four part sums are combined as (t0 + t1) + (t2 + t3) by two butterfly shuffles. Addition commutes, so every lane
 // of the four gets the same bits: a fixed order, whatever the schedule. All 32 lanes of the warp must call it.
+// (mean, rstd) of a row from its sums of u and u^2 over the HID units, every operation rounded explicitly so that
+// each place that computes it (k_rowstat, the fc2 epilogue, the allocation-free fc2) gets the same bits.
+__device__ __forceinline__ float2 rowstat_final(float s, float q)
+{
+    const float mean = __fmul_rn(s, 1.0f / HID);
+    return make_float2(mean, rsqrtf(__fadd_rn(__fsub_rn(__fmul_rn(q, 1.0f / HID), __fmul_rn(mean, mean)), 1e-6f)));
+}
 __device__ __forceinline__ float2 rowstat_of(const float2 *__restrict__ stat, int rows, int row, int j)
 {
     float s = 0.f, q = 0.f;
@@ -36,8 +43,7 @@ __device__ __forceinline__ float2 rowstat_of(const float2 *__restrict__ stat, in
     q += __shfl_xor_sync(0xffffffffu, q, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
     q += __shfl_xor_sync(0xffffffffu, q, 2);
-    const float mean = s * (1.0f / HID);
-    return make_float2(mean, rsqrtf(q * (1.0f / HID) - mean * mean + 1e-6f));
+    return rowstat_final(s, q);
 }
 constexpr int ROWSTAT_THREADS = 256;  // 64 rows per block
 __host__ __device__ constexpr int rowstat_blocks(int rows) { return (rows * 4 + ROWSTAT_THREADS - 1) / ROWSTAT_THREADS; }
@@ -264,7 +270,8 @@ struct EpiFC1 {
 // order into stat[0][row]; the load is issued when the tile starts.
 struct EpiFC2 {
     struct Params {
-        const float2 *ms;
+        const float2 *ms;    // per-row (mean, rstd), or
+        const float2 *part;  // when not null: fc1's NSTAT partials [NSTAT][M], summed here
         const float *c, *d;
         int M;
     };
@@ -272,10 +279,31 @@ struct EpiFC2 {
         float2 ms;
     };
     __device__ __forceinline__ static float col_scale(const Params &, const EpiCtx &) { return 1.0f; }
+    // The thread's row statistics, before the accumulator is ready: either loaded, or summed from the partials in
+    // the order of rowstat_of (partials j, j + 4, ... into sum j, then (s0 + s1) + (s2 + s3)), which gives the same
+    // bits as k_rowstat without its launch. Each load covers 32 consecutive rows (256 bytes) across the warp.
     __device__ __forceinline__ static void begin(const Params &p, const EpiCtx &cx, State &st)
     {
         const int row = cx.row0 + cx.lane;
-        st.ms = row < p.M ? p.ms[row] : make_float2(0.f, 1.f);
+        if (row >= p.M) {
+            st.ms = make_float2(0.f, 1.f);
+        } else if (!p.part) {
+            st.ms = p.ms[row];
+        } else {
+            float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 3
+            for (int g0 = 0; g0 < NSTAT; g0 += 4) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (g0 + j < NSTAT) {
+                        const float2 v = __ldg(p.part + (size_t)(g0 + j) * p.M + row);
+                        s[j] += v.x;
+                        q[j] += v.y;
+                    }
+                }
+            }
+            st.ms = rowstat_final((s[0] + s[1]) + (s[2] + s[3]), (q[0] + q[1]) + (q[2] + q[3]));
+        }
     }
     __device__ __forceinline__ static void apply(const Params &p, const float *acc, const EpiCtx &cx, State &st)
     {

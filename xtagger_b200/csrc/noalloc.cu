@@ -108,6 +108,6 @@ extern "C" int xtb_fc2_noalloc(const uint8_t *h8, int rows, const uint8_t *w, co
     if (!err) return -1;
     k_rowstat_into<<<rowstat_blocks(rows), ROWSTAT_THREADS, 0, st>>>((const float2 *)stat, sc->ms, rows);
     XTB_CK(cudaGetLastError());
-    if (launch_fc2_gemm(A, W, ascale, rows, xm, sc->ms, c, d, err, st)) return -1;
+    if (launch_fc2_gemm(A, W, ascale, rows, xm, sc->ms, nullptr, c, d, err, st)) return -1;
     return 0;
 }

@@ -409,15 +409,14 @@ int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __ha
 {
     CUtensorMap xm;
     if (resid_map(&xm, x, rows)) return -1;
-    XTB_CK(launch_pdl(k_rowstat, dim3(rowstat_blocks(rows)), dim3(ROWSTAT_THREADS), 0, st, (float2 *)stat, rows));
-    XTB_CK(cudaGetLastError());
-    return launch_fc2_gemm(h8, w, ascale, rows, xm, stat, c, d, nullptr, st);
+    // the epilogue sums each row's partials itself (no row-statistics launch; the partials are only read)
+    return launch_fc2_gemm(h8, w, ascale, rows, xm, nullptr, stat, c, d, nullptr, st);
 }
 
 int launch_fc2_gemm(const Operand &h8, const Weight8 &w, float ascale, int rows, const CUtensorMap &xm, const float2 *ms,
-                    const float *c, const float *d, uint32_t *err, cudaStream_t st)
+                    const float2 *part, const float *c, const float *d, uint32_t *err, cudaStream_t st)
 {
-    EpiFC2::Params p{ms, c, d, rows};
+    EpiFC2::Params p{ms, part, c, d, rows};
     return run_proj<EpiFC2, W_FC2>(h8, w, rows, ascale, p, st, &xm, err);
 }
 

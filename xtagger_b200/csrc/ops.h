@@ -75,13 +75,13 @@ int launch_attention(const Attn &a, int nimg, uint8_t *out, float sinv, float vo
 int launch_oproj(const Operand &a, const Weight8 &w, float ascale, int rows, __half *x, cudaStream_t st);
 int launch_fc1(const Operand &h, const Weight8 &w, float ascale, int rows, uint8_t *h8, float2 *stat, const float *rs,
                cudaStream_t st);
-// stat: fc1's [NSTAT][rows] partials; consumed (row (mean, rstd) written into partial 0) before the GEMM.
+// stat: fc1's [NSTAT][rows] partials, only read: the GEMM's epilogue sums each row's partials (EpiFC2::begin).
 int launch_fc2(const Operand &h8, const Weight8 &w, float ascale, int rows, __half *x, float2 *stat, const float *c,
                const float *d, cudaStream_t st);
-// The fc2 GEMM alone, with (mean, rstd) per row already in ms and bounded-wait failures reported in *err: for
-// callers that keep that scratch themselves (xtb_fc2_noalloc). Allocates nothing.
+// The fc2 GEMM alone, with (mean, rstd) per row already in ms (part null), or summed by the epilogue from fc1's
+// partials (part), bounded-wait failures reported in *err (the library's error word when null). Allocates nothing.
 int launch_fc2_gemm(const Operand &h8, const Weight8 &w, float ascale, int rows, const CUtensorMap &xm, const float2 *ms,
-                    const float *c, const float *d, uint32_t *err, cudaStream_t st);
+                    const float2 *part, const float *c, const float *d, uint32_t *err, cudaStream_t st);
 // The fp16 residual x [rows][1024] as the target of TMA reduce-adds.
 int resid_map(CUtensorMap *m, __half *x, int rows);
 int launch_pool_ln(const __half *x, int nimg, const float *g, const float *b, float *pool, __half *pn, uint8_t *pn8,

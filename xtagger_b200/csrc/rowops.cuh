@@ -133,8 +133,8 @@ __global__ void k_selftest_wait(uint64_t ns, int arrive, uint32_t *err)
 // wrote for a row are added in a fixed order (bit-identical run to run, as eva_kernels.cu:205-210) and turned into
 // (mean, rstd) over the 2730 units (eps 1e-6, k_fc2's formula, eva_kernels.cu:318-320), written in place into
 // partial 0 of the row.
-// Each row's (mean, rstd) into partial 0 of stat (consumed by fc2's epilogue). Four threads per row so that small
-// batches still spread the partial loads over the SMs.
+// Each row's (mean, rstd) into partial 0 of stat, for the 2:4-sparse fc2 (the dense fc2's epilogue sums the
+// partials itself, in the same order). Four threads per row so that small batches still spread the partial loads.
 __global__ void __launch_bounds__(ROWSTAT_THREADS) k_rowstat(float2 *__restrict__ stat, int rows)
 {
     griddep_wait();  // the previous kernel of the stream has completed
