@@ -30,6 +30,7 @@ struct GemmArgs {
     float ascale;        // activation dequant scale, folded into every block scale (or into wsu)
     float wsu;           // without PROMOTE: the one weight scale of the tensor (1 for unscaled fp16 operands)
     uint32_t *err;       // library error word
+    int b_weight;        // single-CTA kernel: B is a weight (never written by an earlier kernel), prefetchable
 };
 
 template <int BN, int EW = 8>
@@ -163,22 +164,34 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
-    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
     const int total = g.m_tiles * g.n_tiles;
     const int KI = g.kiters;
+    if (warp != 0) griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
 
     if (warp == 0) {
         if (elect_one()) {
+            // When B is a weight (g.b_weight), the first tile's first ring slots get their B rows before the wait
+            // (first round: no consumer to wait for; the expected bytes include A's), so that their load latency
+            // overlaps the previous kernel's tail.
+            const int pre = (g.b_weight && (int)blockIdx.x < total) ? min(STAGES, KI) : 0;
+            for (int k = 0; k < pre; k++) {
+                mbar_arrive_expect_tx(&full[k], C::STAGE_BYTES);
+                tma_load_2d(sB + k * C::B_BYTES, &tmB, &full[k], k * 128, ((int)blockIdx.x % g.n_tiles) * BN);
+            }
+            griddep_wait();
             int stage = 0;
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 const int nb = t % g.n_tiles, mb = t / g.n_tiles;  // N fastest: an A tile is read by neighbours
                 for (int k = 0; k < KI; k++) {
-                    if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
-                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    const bool early = t == (int)blockIdx.x && k < pre;  // B already on its way
+                    if (!early) {
+                        if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    }
                     tma_load_2d(sA + stage * C::A_BYTES, &tmA, &full[stage], k * 128, mb * 128);
-                    tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], k * 128, nb * BN);
+                    if (!early) tma_load_2d(sB + stage * C::B_BYTES, &tmB, &full[stage], k * 128, nb * BN);
                     if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1;

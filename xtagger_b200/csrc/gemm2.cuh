@@ -96,25 +96,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2CfgT<BN, GROUPS
     cluster_sync();  // the peer's barriers are initialised before anyone arrives on them
     tc_fence_after();
     const uint32_t tbase = *tslot;
-    griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
     const int total = g.m_tiles * g.n_tiles;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     const int KI = g.kiters;
+    if (warp != 0) griddep_wait();  // the previous kernel of the stream has completed: activations may be touched
 
     if (warp == 0) {
         if (elect_one()) {
             const uint32_t full0 = mapa_shared(smem_u32(full), 0);
+            // B is a weight (every launch passes one), never written by an earlier kernel: the first tile's first
+            // ring slots get their B rows before the wait (first round: no consumer to wait for; the expected bytes
+            // include A's), so their load latency overlaps the previous kernel's tail.
+            const int pre = pair < total ? min(STAGES, KI) : 0;
+            for (int k = 0; k < pre; k++) {
+                const uint32_t fb = full0 + k * 8;
+                mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES);
+                tma_load_2d_pair(sB + k * C::B_BYTES, &tmB, fb, k * 128, (pair % g.n_tiles) * C::BN + rank * (C::BN / 2));
+            }
+            griddep_wait();
             int stage = 0;
             uint32_t ph = 0;
             bool ok = true;
             for (int t = pair; t < total && ok; t += npairs) {
                 const int nb = t % g.n_tiles, mb = t / g.n_tiles;  // N fastest: an A tile is read by neighbours
                 for (int k = 0; k < KI; k++) {
-                    if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                    const bool early = t == pair && k < pre;  // B already on its way
                     const uint32_t fb = full0 + stage * 8;
-                    mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES);
+                    if (!early) {
+                        if (!(ok = mbar_wait(&empty[stage], ph ^ 1, g.err, XTB_ERR_WAIT_TMA))) break;
+                        mbar_arrive_expect_tx_cluster(fb, C::STAGE_BYTES);
+                    }
                     tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, fb, k * 128, mb * 256 + rank * 128);
-                    tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, fb, k * 128, nb * C::BN + rank * (C::BN / 2));
+                    if (!early)
+                        tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, fb, k * 128, nb * C::BN + rank * (C::BN / 2));
                     if (++stage == STAGES) {
                         stage = 0;
                         ph ^= 1;

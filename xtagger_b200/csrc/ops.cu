@@ -80,7 +80,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
 static int run_gemm(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
                     const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
-                    uint32_t *err = nullptr, float wsu = 1.0f)
+                    uint32_t *err = nullptr, float wsu = 1.0f, bool b_weight = false)
 {
     using Cfg = GemmCfg<BN>;
     auto kern = k_gemm<Epi, BN, F16, PROMOTE, WS_ON_M>;
@@ -91,7 +91,7 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
         return -1;
     }
     const int dev = current_device();
-    GemmArgs g;
+    GemmArgs g{};
     g.M = M;
     g.N = N;
     g.kiters = (a.row_bytes + 127) / 128;
@@ -103,6 +103,7 @@ static int run_gemm(const Operand &a, const Operand &b, int M, int N, const floa
     g.ascale = ascale;
     g.wsu = wsu;
     g.err = err ? err : error_word(dev);
+    g.b_weight = b_weight ? 1 : 0;
     const int total = g.m_tiles * g.n_tiles;
     int grid = num_sms(dev);
     if (grid > total) grid = total;
@@ -130,7 +131,7 @@ static int run_gemm2(const Operand &a, const Operand &b, int M, int N, const flo
         return -1;
     }
     const int dev = current_device();
-    GemmArgs g;
+    GemmArgs g{};
     g.M = M;
     g.N = N;
     g.kiters = (a.row_bytes + 127) / 128;
@@ -288,7 +289,7 @@ static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, con
             return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
         else
             return run_gemm<Epi, kSingleBN[U], false, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc,
-                                                                    err, w.uniform);
+                                                                    err, w.uniform, true);
     }
     if constexpr (kPairG[U])
         return run_gemm2<Epi, 128, true>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
@@ -296,7 +297,7 @@ static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, con
         return run_gemm2<Epi>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else
         return run_gemm<Epi, kSingleBN[U], false, true, false>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st,
-                                                               tmc, err);
+                                                               tmc, err, 1.0f, true);
 }
 
 // Opt the projection kernel of (Epi, U) into its shared memory and check that its clusters fit (pair kernels).
@@ -331,7 +332,8 @@ int launch_gemm_f32(const Operand &a, const Weight8 &w, float ascale, float *out
 int launch_patch_embed(const Operand &in, const Operand &pe, int nimg, const float *pos, __half *x, cudaStream_t st)
 {
     EpiPatch::Params p{x, pos, nimg * NP};
-    return run_gemm<EpiPatch, 256, true, false, false>(in, pe, nimg * NP, D, nullptr, 0, 1, 1.0f, p, st);
+    return run_gemm<EpiPatch, 256, true, false, false>(in, pe, nimg * NP, D, nullptr, 0, 1, 1.0f, p, st, nullptr,
+                                                       nullptr, 1.0f, true);
 }
 
 int launch_ln_e4m3(const __half *x, const float *g, const float *b, uint8_t *y, int rows, float qs, cudaStream_t st)
@@ -649,7 +651,8 @@ using AttPxG = AttSeq<PX_T, PX_T, (PX_T + 127) / 128>;
 int launch_px_patch(const Operand &in, const Operand &pe, int rows, __half *x, cudaStream_t st)
 {
     EpiPxPatch::Params p{x, rows};
-    return run_gemm<EpiPxPatch, 256, true, false, false>(in, pe, rows, D, nullptr, 0, 1, 1.0f, p, st);
+    return run_gemm<EpiPxPatch, 256, true, false, false>(in, pe, rows, D, nullptr, 0, 1, 1.0f, p, st, nullptr,
+                                                         nullptr, 1.0f, true);
 }
 
 int launch_px_embed(__half *x, const float *pos, const float *w, const float *b, int rows, cudaStream_t st)
