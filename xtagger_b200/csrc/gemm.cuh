@@ -42,8 +42,8 @@ struct GemmCfg {
     static constexpr int EPI_WARPS = EW;   // epilogue warps: EW / 4 per TMEM lane quadrant
     static constexpr int COLS = BN / (EW / 4);  // accumulator columns per epilogue thread
     static constexpr int TBUF = 512 / BN;  // TMEM accumulator buffers (512 columns in all)
-    static constexpr int STAGE_PER_WARP = 32768 / EW;  // staging bytes per epilogue warp
-    static constexpr int STAGING = 32768;
+    static constexpr int STAGE_PER_WARP = 4096;  // staging bytes per epilogue warp
+    static constexpr int STAGING = EW * STAGE_PER_WARP;
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + STAGING + 512;  // + barriers
     static constexpr int THREADS = 64 + 32 * EW;
     static_assert(SMEM <= 232448, "shared memory budget");
@@ -395,23 +395,27 @@ struct EpiF32 {
     static constexpr bool LAST_WIDE = true;
     __device__ __forceinline__ static uint8_t *wide_chunk(uint8_t *w, int r, int c)
     {
-        return w + r * (COLS * 4) + (((c ^ (r & 7)) & (COLS / 4 - 1)) << 4);
+        return w + r * (COLS * 4) + ((c ^ (r & 7)) << 4);  // the XOR stays inside c's aligned group of 8 chunks
     }
     __device__ __forceinline__ static void apply_last(const Params &p, const float *acc, const EpiCtx &cx, State &,
                                                       uint8_t *wide)
     {
-        static_assert(COLS == 64 || COLS == 128, "a warp instruction covers one or two whole rows");
-        constexpr int LPR = COLS / 4;   // lanes per row
+        static_assert(COLS % 32 == 0, "whole 32-column groups");
+        constexpr int GC = (COLS == 64 || COLS == 128) ? COLS : 32;  // columns a lane group covers in one row
+        constexpr int LPR = GC / 4;     // lanes per row
         constexpr int RPI = 32 / LPR;   // rows per instruction
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < COLS / 4; c++)
             *(float4 *)wide_chunk(wide, cx.lane, c) = make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
         __syncwarp();
-        const int sub = cx.lane / LPR, ch = cx.lane % LPR;
-        const int col = cx.col0 + 4 * ch;
         const bool al8 = (p.ld & 1) == 0 && ((uintptr_t)p.out & 7) == 0;
         const bool out16 = ((uintptr_t)p.out & 15) == 0;
+        const int sub = cx.lane / LPR;
+#pragma unroll 1
+        for (int q = 0; q < COLS / GC; q++) {
+        const int ch = q * LPR + cx.lane % LPR;  // the lane's 16-byte chunk of the row
+        const int col = cx.col0 + 4 * ch;
 #pragma unroll 1
         for (int i0 = 0; i0 < 32; i0 += 8 * RPI) {
             float4 v[8];
@@ -435,6 +439,7 @@ struct EpiF32 {
                     if (col + 3 < p.N) o[3] = v[i].w;
                 }
             }
+        }
         }
         __syncwarp();
     }

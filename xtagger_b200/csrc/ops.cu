@@ -77,13 +77,13 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 }
 
 // One launch of the tcgen05 GEMM: A = a (M rows), B = b (N rows), K slices of 128 bytes.
-template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M>
+template <class Epi, int BN, bool F16, bool PROMOTE, bool WS_ON_M, int EW = 8>
 static int run_gemm(const Operand &a, const Operand &b, int M, int N, const float *ws, int ws_ld, int ws_rows, float ascale,
                     const typename Epi::Params &ep, cudaStream_t st, const CUtensorMap *tmc = nullptr,
                     uint32_t *err = nullptr, float wsu = 1.0f, bool b_weight = false)
 {
-    using Cfg = GemmCfg<BN>;
-    auto kern = k_gemm<Epi, BN, F16, PROMOTE, WS_ON_M>;
+    using Cfg = GemmCfg<BN, EW>;
+    auto kern = k_gemm<Epi, BN, F16, PROMOTE, WS_ON_M, EW>;
     if (set_smem((const void *)kern, Cfg::SMEM)) return -1;
     if (a.row_bytes != b.row_bytes || M <= 0 || N <= 0 || a.box_rows != A_BOX_ROWS || b.box_rows != BN) {
         fprintf(stderr, "eva: gemm operands (K bytes %d vs %d, boxes %d / %d rows, M %d, N %d)\n", a.row_bytes,
@@ -268,11 +268,15 @@ static constexpr bool kPair[5] = {(XTB_PAIR_MASK & 1) != 0 && !kPairG[0], (XTB_P
 
 // Tile width of the single-CTA GEMM per weight use: 256 for the forward's projections; the stand-alone fp32-output
 // GEMM (W_F32) takes XTB_F32_BN.
+// 192 runs on 12 epilogue warps (three per TMEM lane quadrant, 64 columns each, so that no thread's columns straddle
+// a 128-column block of weight scales): 135 tiles of 128 x 192 for config 1's 1025 x 2730 instead of 99 of 128 x 256.
 #ifndef XTB_F32_BN
-#define XTB_F32_BN 256
+#define XTB_F32_BN 192
 #endif
+static constexpr int kF32EW = XTB_F32_BN == 192 ? 12 : 8;
 static constexpr int kSingleBN[5] = {256, 256, 256, 256, XTB_F32_BN};
-using EpiF32Out = EpiF32<XTB_F32_BN / 2>;
+static constexpr int kSingleEW[5] = {8, 8, 8, 8, kF32EW};
+using EpiF32Out = EpiF32<XTB_F32_BN / (kF32EW / 4)>;
 
 int weight_box_rows(WeightUse u) { return kPairG[u] ? Gemm2GCfg::BN / 2 : kPair[u] ? Gemm2Cfg::BN / 2 : kSingleBN[u]; }
 
@@ -288,16 +292,16 @@ static int run_proj(const Operand &a, const Weight8 &w, int M, float ascale, con
         if constexpr (kPair[U])
             return run_gemm2<Epi, 256, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc, err, w.uniform);
         else
-            return run_gemm<Epi, kSingleBN[U], false, false, false>(a, w.op, M, w.n, nullptr, 0, 1, ascale, ep, st, tmc,
-                                                                    err, w.uniform, true);
+            return run_gemm<Epi, kSingleBN[U], false, false, false, kSingleEW[U]>(a, w.op, M, w.n, nullptr, 0, 1, ascale,
+                                                                                  ep, st, tmc, err, w.uniform, true);
     }
     if constexpr (kPairG[U])
         return run_gemm2<Epi, 128, true>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else if constexpr (kPair[U])
         return run_gemm2<Epi>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st, tmc, err);
     else
-        return run_gemm<Epi, kSingleBN[U], false, true, false>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n), ascale, ep, st,
-                                                               tmc, err, 1.0f, true);
+        return run_gemm<Epi, kSingleBN[U], false, true, false, kSingleEW[U]>(a, w.op, M, w.n, w.ws, kb(w.k), kb(w.n),
+                                                                             ascale, ep, st, tmc, err, 1.0f, true);
 }
 
 // Opt the projection kernel of (Epi, U) into its shared memory and check that its clusters fit (pair kernels).
@@ -316,8 +320,10 @@ static int prepare_proj()
                    ? -1
                    : 0;
     } else {
-        return set_smem((const void *)k_gemm<Epi, kSingleBN[U], false, true, false>, GemmCfg<kSingleBN[U]>::SMEM) ||
-                       set_smem((const void *)k_gemm<Epi, kSingleBN[U], false, false, false>, GemmCfg<kSingleBN[U]>::SMEM)
+        return set_smem((const void *)k_gemm<Epi, kSingleBN[U], false, true, false, kSingleEW[U]>,
+                        GemmCfg<kSingleBN[U], kSingleEW[U]>::SMEM) ||
+                       set_smem((const void *)k_gemm<Epi, kSingleBN[U], false, false, false, kSingleEW[U]>,
+                                GemmCfg<kSingleBN[U], kSingleEW[U]>::SMEM)
                    ? -1
                    : 0;
     }
@@ -325,8 +331,19 @@ static int prepare_proj()
 
 int launch_gemm_f32(const Operand &a, const Weight8 &w, float ascale, float *out, int ldo, cudaStream_t st)
 {
+    if (w.sf) {  // power-of-two block scales: the block-scaled kernels, 128 accumulator columns per epilogue thread
+        EpiF32<128>::Params p{out, ldo, a.rows, w.n};
+        return !w.sf_pair ? run_gemm_mx<EpiF32<128>>(a, w, a.rows, ascale, p, st)
+               : w.sf_wide ? run_gemm2_mx<EpiF32<128>, 2>(a, w, a.rows, ascale, p, st)
+                           : run_gemm2_mx<EpiF32<128>, 1>(a, w, a.rows, ascale, p, st);
+    }
+    // fp32 block scales (or one per tensor): the single-CTA kernel on XTB_F32_BN-wide tiles
     EpiF32Out::Params p{out, ldo, a.rows, w.n};
-    return run_proj<EpiF32Out, W_F32>(a, w, a.rows, ascale, p, st);
+    if (w.uniform > 0.0f)
+        return run_gemm<EpiF32Out, XTB_F32_BN, false, false, false, kF32EW>(a, w.op, a.rows, w.n, nullptr, 0, 1, ascale,
+                                                                          p, st, nullptr, nullptr, w.uniform, true);
+    return run_gemm<EpiF32Out, XTB_F32_BN, false, true, false, kF32EW>(a, w.op, a.rows, w.n, w.ws, kb(w.k), kb(w.n),
+                                                                     ascale, p, st, nullptr, nullptr, 1.0f, true);
 }
 
 int launch_patch_embed(const Operand &in, const Operand &pe, int nimg, const float *pos, __half *x, cudaStream_t st)
