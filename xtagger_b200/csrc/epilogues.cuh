@@ -338,21 +338,30 @@ struct EpiPatch {
             __syncwarp();
             const int w = (cx.lane & 15) * 2;
             const int col = cx.col0 + 32 * c + w;
-            float2 sv[16];  // all staged values first, then the loads of pos and the stores (see EpiF32::apply)
+            // two rounds of eight row pairs: each round's staged values and position rows are all loaded before its
+            // stores, so eight position loads (L2) are in flight at a time and each round waits out one latency
+#pragma unroll 1
+            for (int h = 0; h < 2; h++) {
+                float2 sv[8], ps[8];
 #pragma unroll
-            for (int i = 0; i < 16; i++) sv[i] = stage_f32x2(cx.stage, 2 * i + (cx.lane >> 4), w);
-#pragma unroll 4
-            for (int i = 0; i < 16; i++) {
-                const int r = 2 * i + (cx.lane >> 4), rw = cx.row0 + r;
-                if (rw < p.M) {
-                    const int b = rw >> 10, pp = rw & 1023;
-                    const float2 a = sv[i];
-                    const float2 ps = *(const float2 *)(p.pos + (size_t)(1 + pp) * D + col);
-                    const float2 ah = __half22float2(__floats2half2_rn(a.x, a.y));
-                    *(__half2 *)(p.x + ((size_t)b * T + 1 + pp) * D + col) = __floats2half2_rn(ah.x + ps.x, ah.y + ps.y);
-                    if (pp == 0) {
-                        const float2 p0 = *(const float2 *)(p.pos + col);
-                        *(__half2 *)(p.x + (size_t)b * T * D + col) = __floats2half2_rn(p0.x, p0.y);
+                for (int i = 0; i < 8; i++) {
+                    const int r = 2 * (8 * h + i) + (cx.lane >> 4), rw = cx.row0 + r;
+                    sv[i] = stage_f32x2(cx.stage, r, w);
+                    ps[i] = rw < p.M ? __ldg((const float2 *)(p.pos + (size_t)(1 + (rw & 1023)) * D + col))
+                                     : make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int r = 2 * (8 * h + i) + (cx.lane >> 4), rw = cx.row0 + r;
+                    if (rw < p.M) {
+                        const int b = rw >> 10, pp = rw & 1023;
+                        const float2 ah = __half22float2(__floats2half2_rn(sv[i].x, sv[i].y));
+                        *(__half2 *)(p.x + ((size_t)b * T + 1 + pp) * D + col) =
+                            __floats2half2_rn(ah.x + ps[i].x, ah.y + ps[i].y);
+                        if (pp == 0) {
+                            const float2 p0 = __ldg((const float2 *)(p.pos + col));
+                            *(__half2 *)(p.x + (size_t)b * T * D + col) = __floats2half2_rn(p0.x, p0.y);
+                        }
                     }
                 }
             }
